@@ -1,0 +1,294 @@
+// tcgen05 GEMM instantiations with the Flow-specific fused epilogues, the
+// causal grouped conv-pos kernel, and tensor-map creation.
+#include <cstdio>
+#include <mutex>
+
+#include "gemm.cuh"
+#include "kernels.h"
+
+namespace lx {
+
+// ---------------------------------------------------------------------------
+// device / tensor-map plumbing
+// ---------------------------------------------------------------------------
+int num_sms() {
+  static int cache[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (cache[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = n > 0 ? n : 148;
+  }
+  return cache[dev];
+}
+
+typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static PFN_encodeTiled get_encode() {
+  static PFN_encodeTiled fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_encodeTiled>(p);
+  });
+  return fn;
+}
+
+bool tmap_bf16(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows,
+               uint32_t box_cols) {
+  PFN_encodeTiled enc = get_encode();
+  if (!enc) return false;
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || (ld * 2) % 16 != 0) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld * 2};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   box_cols * 2 == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// ---------------------------------------------------------------------------
+// epilogues: called per (row, 16 consecutive columns) with fp32 accumulators
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void store_bf16x16(bf16* dst, const float (&v)[16]) {
+  uint4 a, b;
+  a.x = pack_bf16x2(v[0], v[1]);
+  a.y = pack_bf16x2(v[2], v[3]);
+  a.z = pack_bf16x2(v[4], v[5]);
+  a.w = pack_bf16x2(v[6], v[7]);
+  b.x = pack_bf16x2(v[8], v[9]);
+  b.y = pack_bf16x2(v[10], v[11]);
+  b.z = pack_bf16x2(v[12], v[13]);
+  b.w = pack_bf16x2(v[14], v[15]);
+  reinterpret_cast<uint4*>(dst)[0] = a;
+  reinterpret_cast<uint4*>(dst)[1] = b;
+}
+
+__device__ __forceinline__ void add_bias16(float (&v)[16], const float* bias) {
+  const float4* b4 = reinterpret_cast<const float4*>(bias);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float4 b = __ldg(b4 + j);
+    v[4 * j + 0] += b.x;
+    v[4 * j + 1] += b.y;
+    v[4 * j + 2] += b.z;
+    v[4 * j + 3] += b.w;
+  }
+}
+
+struct EpiQKV {
+  const float* bias;
+  bf16* q;
+  bf16* k;
+  __half* vt;  // V^T in fp16: the B operand of the attention PV MMA
+  int ldvt;
+  const int* pos;
+  const float2* rope;  // [pos][32] (cos, sin)
+  __device__ __forceinline__ void operator()(int row, int col0, float (&v)[16]) const {
+    add_bias16(v, bias + col0);
+    const int which = col0 >> 10;
+    const int c = col0 & (DIM - 1);
+    if (which < 2) {
+      if (c < HDIM) {
+        // partial rotary, GPT-J pairs (2i, 2i+1), angle pos * inv_freq[i]
+        const float2* cs = rope + static_cast<size_t>(__ldg(pos + row)) * 32 + (c >> 1);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float2 t = __ldg(cs + i);
+          const float x0 = v[2 * i], x1 = v[2 * i + 1];
+          v[2 * i] = x0 * t.x - x1 * t.y;
+          v[2 * i + 1] = x1 * t.x + x0 * t.y;
+        }
+      }
+      store_bf16x16((which == 0 ? q : k) + static_cast<size_t>(row) * DIM + c, v);
+    } else {
+      __half* dst = vt + static_cast<size_t>(c) * ldvt + row;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) dst[static_cast<size_t>(j) * ldvt] = __float2half_rn(v[j]);
+    }
+  }
+};
+
+struct EpiGateRes {
+  const float* bias;
+  const float* gate;
+  float* x;
+  __device__ __forceinline__ void operator()(int row, int col0, float (&v)[16]) const {
+    float4* xr = reinterpret_cast<float4*>(x + static_cast<size_t>(row) * DIM + col0);
+    const float4* b4 = reinterpret_cast<const float4*>(bias + col0);
+    const float4* g4 = reinterpret_cast<const float4*>(gate + col0);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float4 xv = xr[j];
+      const float4 b = __ldg(b4 + j);
+      const float4 g = __ldg(g4 + j);
+      xv.x += g.x * (v[4 * j + 0] + b.x);
+      xv.y += g.y * (v[4 * j + 1] + b.y);
+      xv.z += g.z * (v[4 * j + 2] + b.z);
+      xv.w += g.w * (v[4 * j + 3] + b.w);
+      xr[j] = xv;
+    }
+  }
+};
+
+struct EpiGelu {
+  const float* bias;
+  bf16* h;
+  __device__ __forceinline__ void operator()(int row, int col0, float (&v)[16]) const {
+    add_bias16(v, bias + col0);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = gelu_tanh_f(v[j]);
+    store_bf16x16(h + static_cast<size_t>(row) * FF + col0, v);
+  }
+};
+
+struct EpiF32 {
+  const float* bias;
+  float* out;
+  int ldo;
+  __device__ __forceinline__ void operator()(int row, int col0, float (&v)[16]) const {
+    if (bias) add_bias16(v, bias + col0);
+    float4* o = reinterpret_cast<float4*>(out + static_cast<size_t>(row) * ldo + col0);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) o[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+  }
+};
+
+struct EpiInProj {
+  const float* cst;
+  float* x;
+  bf16* stage;
+  const int* p2s;
+  __device__ __forceinline__ void operator()(int row, int col0, float (&v)[16]) const {
+    const float4* c4 = reinterpret_cast<const float4*>(cst + static_cast<size_t>(row) * DIM + col0);
+    float4* xr = reinterpret_cast<float4*>(x + static_cast<size_t>(row) * DIM + col0);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float4 c = c4[j];
+      v[4 * j + 0] += c.x;
+      v[4 * j + 1] += c.y;
+      v[4 * j + 2] += c.z;
+      v[4 * j + 3] += c.w;
+      xr[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    }
+    const int srow = __ldg(p2s + row);
+    if (srow >= 0) store_bf16x16(stage + static_cast<size_t>(srow) * DIM + col0, v);
+  }
+};
+
+struct EpiConv {
+  const float* bias;
+  int second;
+  bf16* out_stage;
+  float* x;
+  const int* s2p;
+  __device__ __forceinline__ void operator()(int srow, int col0, float (&v)[16]) const {
+    const int prow = __ldg(s2p + srow);
+    if (prow < 0) return;  // zero gap rows of the staging layout stay zero
+    add_bias16(v, bias + col0);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = mish_f(v[j]);
+    if (!second) {
+      store_bf16x16(out_stage + static_cast<size_t>(srow) * DIM + col0, v);
+    } else {
+      float4* xr = reinterpret_cast<float4*>(x + static_cast<size_t>(prow) * DIM + col0);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float4 xv = xr[j];
+        xv.x += v[4 * j + 0];
+        xv.y += v[4 * j + 1];
+        xv.z += v[4 * j + 2];
+        xv.w += v[4 * j + 3];
+        xr[j] = xv;
+      }
+    }
+  }
+};
+
+// ---------------------------------------------------------------------------
+// launch helper
+// ---------------------------------------------------------------------------
+template <int BN, int STAGES, int MODE, class Epi>
+static void launch(const CUtensorMap& A, const CUtensorMap& B, int M, int N, int K, int b_off, const Epi& epi,
+                   int* err, cudaStream_t s) {
+  constexpr int smem = gemm_smem_bytes<BN, STAGES>();
+  static bool attr_done[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_done[dev & 63]) {
+    cudaFuncSetAttribute(k_gemm<BN, STAGES, MODE, Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    attr_done[dev & 63] = true;
+  }
+  const int tiles = ((M + GEMM_BM - 1) / GEMM_BM) * ((N + BN - 1) / BN);
+  int grid = num_sms();
+  if (tiles < grid) grid = tiles;
+  if (grid <= 0) return;
+  GemmShape sh{M, N, K, b_off, err};
+  k_gemm<BN, STAGES, MODE, Epi><<<grid, GEMM_THREADS, smem, s>>>(A, B, sh, epi);
+}
+
+template <class Epi>
+static void launch_bn(int bn, const CUtensorMap& A, const CUtensorMap& B, int M, int N, int K, int b_off,
+                      const Epi& e, int* err, cudaStream_t s) {
+  if (bn == 256)
+    launch<256, 4, MODE_GEMM>(A, B, M, N, K, b_off, e, err, s);
+  else
+    launch<128, 6, MODE_GEMM>(A, B, M, N, K, b_off, e, err, s);
+}
+
+int pick_bn(int M, int N) {
+  if (N % 256 != 0) return 128;
+  const long tiles256 = static_cast<long>((M + 127) / 128) * (N / 256);
+  return tiles256 >= 2L * num_sms() ? 256 : 128;
+}
+
+void gemm_qkv(int bn, const CUtensorMap& A, const CUtensorMap& B, int M, int b_off, const float* bias, bf16* q,
+              bf16* k, __half* vt, int ldvt, const int* pos, const float2* rope, int* err, cudaStream_t s) {
+  EpiQKV e{bias, q, k, vt, ldvt, pos, rope};
+  launch_bn(bn, A, B, M, QKV_N, DIM, b_off, e, err, s);
+}
+
+void gemm_gate_res(int bn, const CUtensorMap& A, const CUtensorMap& B, int M, int K, int b_off, const float* bias,
+                   const float* gate, float* x, int* err, cudaStream_t s) {
+  EpiGateRes e{bias, gate, x};
+  launch_bn(bn, A, B, M, DIM, K, b_off, e, err, s);
+}
+
+void gemm_gelu(int bn, const CUtensorMap& A, const CUtensorMap& B, int M, int b_off, const float* bias, bf16* h,
+               int* err, cudaStream_t s) {
+  EpiGelu e{bias, h};
+  launch_bn(bn, A, B, M, FF, DIM, b_off, e, err, s);
+}
+
+void gemm_f32(int bn, const CUtensorMap& A, const CUtensorMap& B, int M, int N, int K, const float* bias,
+              float* out, int ldo, int* err, cudaStream_t s) {
+  EpiF32 e{bias, out, ldo};
+  if (N == MEL)
+    launch<80, 7, MODE_GEMM>(A, B, M, N, K, 0, e, err, s);
+  else
+    launch_bn(bn, A, B, M, N, K, 0, e, err, s);
+}
+
+void gemm_in_proj(int bn, const CUtensorMap& A, const CUtensorMap& B, int M, const float* cst, float* x,
+                  bf16* stage, const int* p2s, int* err, cudaStream_t s) {
+  EpiInProj e{cst, x, stage, p2s};
+  launch_bn(bn, A, B, M, DIM, MEL, 0, e, err, s);
+}
+
+void conv_pos(const CUtensorMap& A, const CUtensorMap& B, int Ms, const float* bias, int second, bf16* out_stage,
+              float* x, const int* s2p, int* err, cudaStream_t s) {
+  EpiConv e{bias, second, out_stage, x, s2p};
+  launch<64, 8, MODE_CONV>(A, B, Ms, DIM, 0, 0, e, err, s);
+}
+
+}  // namespace lx

@@ -1,0 +1,205 @@
+// Persistent warp-specialised tcgen05 GEMM for sm_100a.
+//
+//   D[M, N] = A[M, K] * B[N, K]^T      (A, B bf16, K-major; fp32 accumulate)
+//
+// One CTA per SM walks a static list of 128 x BN output tiles.  Roles:
+//   warp 0      TMA producer: 128x64 A box + BNx64 B box per stage
+//               (128-byte swizzle) into a STAGES-deep shared-memory ring
+//   warp 1      TMEM allocator; lane 0 issues tcgen05.mma (M=128, N=BN, K=16)
+//               and tcgen05.commit to release ring slots / publish tiles
+//   warps 2..5  epilogue: tcgen05.ld of a 32-row TMEM lane quarter each,
+//               fused element-wise epilogue, direct global stores
+// The fp32 accumulator is double-buffered in tensor memory (2 x BN columns),
+// so the epilogue of tile i overlaps the MMAs of tile i+1.
+//
+// MODE_CONV turns the same pipeline into the causal grouped Conv1d of the
+// DiT's position embedding (k = 31, 16 groups of 64 channels): the K loop runs
+// over the 31 taps, the A box of tap k is the 128-row activation tile shifted
+// by k - 30 rows (TMA row coordinate; rows before the buffer start read as
+// zero, rows before each sequence are zero gap rows of the staging layout),
+// and the B box is the [64 out x 64 in] weight slice of (group, tap).
+#pragma once
+
+#include "common.cuh"
+
+namespace lx {
+
+enum GemmMode : int { MODE_GEMM = 0, MODE_CONV = 1 };
+
+constexpr int GEMM_BM = 128;
+constexpr int GEMM_BK = 64;
+constexpr int GEMM_THREADS = 192;
+constexpr int CONV_TAPS = 31;
+
+struct GemmShape {
+  int M, N, K;
+  int b_off;  // row offset into the B tensor (layer slice of stacked weights)
+  int* err;   // device error word
+};
+
+__host__ __device__ constexpr int tmem_cols_for(int bn) {
+  return (2 * bn) <= 32 ? 32 : (2 * bn) <= 64 ? 64 : (2 * bn) <= 128 ? 128 : (2 * bn) <= 256 ? 256 : 512;
+}
+
+template <int BN, int STAGES>
+__host__ __device__ constexpr int gemm_smem_bytes() {
+  return 1024 /*alignment slack*/ + STAGES * (GEMM_BM * GEMM_BK * 2 + BN * GEMM_BK * 2) + 256 /*barriers*/;
+}
+
+template <int BN, int STAGES, int MODE, class Epi>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmShape sh,
+           Epi epi) {
+  static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M=128 must be a multiple of 16 in [16,256]");
+  constexpr int A_BYTES = GEMM_BM * GEMM_BK * 2;
+  constexpr int B_BYTES = BN * GEMM_BK * 2;
+  constexpr uint32_t TMEM_COLS = tmem_cols_for(BN);
+  constexpr uint32_t IDESC = idesc_bf16_f32(GEMM_BM, BN);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 4);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int tiles_n = (sh.N + BN - 1) / BN;
+  const int tiles_m = (sh.M + GEMM_BM - 1) / GEMM_BM;
+  const int n_tiles = tiles_m * tiles_n;
+  const int num_kb = (MODE == MODE_CONV) ? CONV_TAPS : (sh.K + GEMM_BK - 1) / GEMM_BK;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+        const int m0 = (tile / tiles_n) * GEMM_BM;
+        const int n0 = (tile % tiles_n) * BN;
+        bool ok = true;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, sh.err, abort_flag, DEV_TIMEOUT_PRODUCER)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], A_BYTES + B_BYTES);
+          if (MODE == MODE_CONV) {
+            // group g = n0 / 64; tap kb
+            tma_load_2d(sA + stage * A_BYTES, &tmA, &full[stage], n0, m0 - (CONV_TAPS - 1) + kb);
+            tma_load_2d(sB + stage * B_BYTES, &tmB, &full[stage], 0, sh.b_off + ((n0 / 64) * CONV_TAPS + kb) * 64);
+          } else {
+            tma_load_2d(sA + stage * A_BYTES, &tmA, &full[stage], kb * GEMM_BK, m0);
+            tma_load_2d(sB + stage * B_BYTES, &tmB, &full[stage], kb * GEMM_BK, sh.b_off + n0);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, sh.err, abort_flag, DEV_TIMEOUT_MMA)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        bool ok = true;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, sh.err, abort_flag, DEV_TIMEOUT_MMA)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + stage * A_BYTES);
+          const uint32_t b_addr = smem_u32(sB + stage * B_BYTES);
+#pragma unroll
+          for (int k = 0; k < GEMM_BK / 16; ++k) {
+            umma_ss(d_tmem, sdesc_sw128(a_addr + k * 32), sdesc_sw128(b_addr + k * 32), IDESC,
+                    (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+    }
+  } else {
+    // epilogue warps 2..5 -> TMEM lane quarters 2,3,0,1
+    const int q = warp & 3;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+      const int m0 = (tile / tiles_n) * GEMM_BM;
+      const int n0 = (tile % tiles_n) * BN;
+      bool ok = mbar_wait(&tfull[acc], acc_phase, sh.err, abort_flag, DEV_TIMEOUT_EPILOGUE);
+      if (!__all_sync(0xffffffffu, ok)) break;  // warp-uniform exit before the .sync.aligned loads
+      tc_fence_after();
+      const int row = m0 + q * 32 + lane;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        float v[16];
+        tmem_ld16(t_row + c0, v);
+        tmem_ld_wait();
+        if (row < sh.M && n0 + c0 < sh.N) epi(row, n0 + c0, v);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+}  // namespace lx

@@ -1,0 +1,127 @@
+// Host-side interface of the Flow kernels (launchers).  All launches are
+// asynchronous on the given stream; every kernel that waits on an mbarrier
+// reports a timeout through the device error word `err`.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace lx {
+
+typedef __nv_bfloat16 bf16;
+
+constexpr int DIM = 1024;
+constexpr int FF = 2048;
+constexpr int MEL = 80;
+constexpr int HEADS = 16;
+constexpr int HDIM = 64;
+constexpr int DEPTH = 22;
+constexpr int QKV_N = 3 * DIM;
+constexpr int MOD_N = 6 * DIM;
+constexpr int CONV_K = 31;
+constexpr int CONV_G = 16;
+constexpr int COND_K = 3 * MEL;  // [cond, mu, spks] columns of the input projection
+
+// Number of SMs of the current device (cached per device).
+int num_sms();
+
+// 2-D tensor map over 16-bit elements (bf16, or fp16 data: TMA copies bits):
+// `rows` x `cols` elements, row stride `ld` elements, box = box_rows x
+// box_cols (box_cols * 2 == 128 selects the 128B swizzle).
+bool tmap_bf16(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows,
+               uint32_t box_cols);
+
+struct AttnTile {
+  int seq_start;  // first packed row of the sequence
+  int seq_len;    // valid frames of the sequence
+  int q0;         // first query of this tile, relative to seq_start
+  int pad;
+};
+
+// ---- GEMMs (tcgen05) --------------------------------------------------------
+// `bn` is the N tile (128 or 256; pick_bn chooses by wave count); the B tensor
+// map's box must be bn x 64.  `b_off` selects the layer slice of stacked
+// weights (row offset into B).
+int pick_bn(int M, int N);
+// q/k [M,1024] bf16 with bias + partial rotary on channels 0..63; v written
+// transposed to vt[1024][ldvt] in fp16 (the PV operand of the attention).
+void gemm_qkv(int bn, const CUtensorMap& A, const CUtensorMap& B, int M, int b_off, const float* bias, bf16* q,
+              bf16* k, __half* vt, int ldvt, const int* pos, const float2* rope, int* err, cudaStream_t s);
+// x[M,1024] += gate[col] * (A*B^T + bias)
+void gemm_gate_res(int bn, const CUtensorMap& A, const CUtensorMap& B, int M, int K, int b_off, const float* bias,
+                   const float* gate, float* x, int* err, cudaStream_t s);
+// h[M,2048] = bf16(gelu_tanh(A*B^T + bias))
+void gemm_gelu(int bn, const CUtensorMap& A, const CUtensorMap& B, int M, int b_off, const float* bias, bf16* h,
+               int* err, cudaStream_t s);
+// out[M,N] (row stride ldo) = A*B^T + bias (bias may be null).  N == 80 uses an
+// 80-wide tile (B box 80 x 64) and ignores bn.
+void gemm_f32(int bn, const CUtensorMap& A, const CUtensorMap& B, int M, int N, int K, const float* bias,
+              float* out, int ldo, int* err, cudaStream_t s);
+// x-part of the input projection: v = A*B^T + cst; x = v; stage[p2s[row]] = bf16(v)
+void gemm_in_proj(int bn, const CUtensorMap& A, const CUtensorMap& B, int M, const float* cst, float* x,
+                  bf16* stage, const int* p2s, int* err, cudaStream_t s);
+// causal grouped conv (k=31, 16 groups) over the staged rows [0, Ms); B box 64 x 64.
+// second == 0: out_stage[srow] = bf16(mish(conv + bias))  (rows with s2p >= 0)
+// second == 1: x[s2p[srow]] += mish(conv + bias)
+void conv_pos(const CUtensorMap& A, const CUtensorMap& B, int Ms, const float* bias, int second, bf16* out_stage,
+              float* x, const int* s2p, int* err, cudaStream_t s);
+
+// ---- attention (tcgen05 flash attention) -----------------------------------
+// out[row, 64h..64h+63] for every valid query row of every tile; chunk > 0
+// applies the block-causal chunk mask, keys >= seq_len are always masked.
+void attention(const CUtensorMap& Q, const CUtensorMap& K, const CUtensorMap& Vt, const AttnTile* tiles,
+               int n_tiles, int chunk, bf16* out, int* err, cudaStream_t s);
+
+// ---- element-wise / row kernels -----------------------------------------
+// y = bf16(LN(x) * (1 + scale) + shift), rows of 1024 fp32.
+void adaln_rows(const float* x, bf16* y, const float* shift, const float* scale, int R, cudaStream_t s);
+// x_state[f, c] += dt * (1.7 dphi[row_c] - 0.7 dphi[row_u]); xb rows <- bf16(x_state)
+void euler_update(float* xs, const float* dphi, const int2* frame_rows, bf16* xb, int F, float dt, float cfg,
+                  cudaStream_t s);
+// x_state[f, c] = noise[src.x + c * src.y]; xb rows <- bf16
+void init_state(float* xs, const float* noise, const int2* frame_rows, const int2* frame_src, bf16* xb, int F,
+                cudaStream_t s);
+// a_cond[row_c, 0:240] = bf16([cond, mu, spks]) from [u][80][T] inputs
+void gather_cond(bf16* a_cond, const float* cond, const float* mu, const float* spks, const int2* frame_rows,
+                 const int2* frame_src, const int* frame_utt, int F, cudaStream_t s);
+// zero the staging rows with s2p < 0 in both conv staging buffers
+void zero_gap_rows(bf16* a, bf16* b, const int* s2p, int Rs, cudaStream_t s);
+// mel[src.x + c * src.y] = x_state[f, c]
+void scatter_mel(float* mel, const float* xs, const int2* frame_src, int F, cudaStream_t s);
+// copy fp32 rows of 1024 from packed rows to a [B, T, 1024] capture (row -> dst index)
+void gather_rows(float* dst, const float* src, const int* rows, int n, int width, cudaStream_t s);
+void gather_rows_bf16(float* dst, const bf16* src, const int* rows, int n, int width, cudaStream_t s);
+
+// out[s][n] = act_out(sum_k act_in(in[s][k]) * W[n][k] + b[n]), S <= 16 rows, fp32.
+// act: 0 none, 1 SiLU.
+void gemv_rows(const float* in, int S, int K, const float* W, const float* b, int N, float* out, int ldo,
+               int act_in, int act_out, cudaStream_t s);
+// sinusoidal timestep embedding (256) of S timesteps.
+void sinus_embed(const float* t, int S, float* out, cudaStream_t s);
+// fp32 -> bf16 conversion
+void to_bf16(const float* src, bf16* dst, size_t n, cudaStream_t s);
+
+// ---- frontend (once per utterance) -----------------------------------------
+void frontend_spk(const float* emb192, const float* w, const float* b, float* spk80, cudaStream_t s);
+void frontend_embed(const int* tok, int n, const float* table, int vocab, float* out, cudaStream_t s);
+void frontend_conv1(const float* emb, int n, const float* w, const float* b, float* h, cudaStream_t s);
+void frontend_conv2(const float* h, const float* emb, int n, const float* w, const float* b, float* out,
+                    cudaStream_t s);
+// mu[c][2t + r] = pre[t][c]; cond[c][t] = t < mel_len1 ? prompt_feat[t][c] : 0
+void frontend_mu_cond(const float* pre, int n_tok, const float* prompt_feat, int mel_len1, float* mu, float* cond,
+                      cudaStream_t s);
+
+// ---- standalone fused ops (microbench) ------------------
+void op_adaln_f32(const float* x, float* y, const float* shift, const float* scale, int R, cudaStream_t s);
+void op_adaln_bf16(const bf16* x, float* y, const float* shift, const float* scale, int R, cudaStream_t s);
+void op_gate_res_f32(float* x, const float* y, const float* gate, int R, cudaStream_t s);
+void op_gate_res_bf16(float* x, const bf16* y, const float* gate, int R, cudaStream_t s);
+void op_rotary_f32(const float* x, float* y, const int* pos, const float2* rope, int R, cudaStream_t s);
+void op_rotary_bf16(const bf16* x, float* y, const int* pos, const float2* rope, int R, cudaStream_t s);
+void op_gelu_f32(const float* x, float* y, size_t n, cudaStream_t s);
+void op_gelu_bf16(const bf16* x, float* y, size_t n, cudaStream_t s);
+
+}  // namespace lx

@@ -1,0 +1,164 @@
+"""End-to-end parity of the CUDA Flow path (through the C ABI) against the
+oracle and the reference's golden vectors.
+
+Tolerances (north star): per-stage rel-max (max|d| / max|ref|, the
+reference's own stage metric, tests/verify_flow.py:57-66) within the
+reference's GREEN gate of 1e-2, and final mel max-abs <= 2e-2 after all 10
+Euler steps with bf16 activations / fp32 accumulation and residual stream.
+"""
+
+import os
+
+import numpy as np
+import pytest
+
+from conftest import golden, rel_l2, rel_max
+from oracle import flow_oracle as fo
+
+pytestmark = pytest.mark.gpu
+
+STAGE_TOL = 1e-2     # reference GREEN gate per stage (README.md:187-199)
+MEL_ABS_TOL = 2e-2   # final mel max-abs after 10 steps (north star)
+
+
+@pytest.fixture(scope="module")
+def gguf_path(tmp_path_factory):
+    from larynx_b200.weights import write_synthetic_gguf
+    p = str(tmp_path_factory.mktemp("w") / "flow_synth.gguf")
+    write_synthetic_gguf(p, seed=0, std=0.02)
+    return p
+
+
+@pytest.fixture(scope="module")
+def dec(gguf_path):
+    torch = pytest.importorskip("torch")
+    assert torch.cuda.is_available()
+    from larynx_b200 import FlowDecoder
+    d = FlowDecoder(0)
+    assert d.load(gguf_path), d.last_error
+    yield d
+    d.close()
+
+
+def _flat(a):
+    return np.concatenate([np.asarray(x, np.float32).reshape(-1) for x in a])
+
+
+def _split(flat, lengths):
+    out, o = [], 0
+    for L in lengths:
+        out.append(flat[o:o + 80 * L].reshape(80, L))
+        o += 80 * L
+    return out
+
+
+def test_estimator_stages_fixture(dec, weights):
+    """One DiT forward of the reference fixture's step-1 batch ([x; x] rows)."""
+    g = golden("flow_fixture.npz")
+    T = g["mu"].shape[-1]
+    x = g["noise_z"][0]
+    mu = g["mu"][0]
+    cond = g["cond"][0]
+    spk = g["spk"][0]
+    xs = [x, x]
+    mus = [mu, np.zeros_like(mu)]
+    conds = [cond, np.zeros_like(cond)]
+    spks = np.stack([spk, np.zeros_like(spk)])
+    for blk in (0, 10, 21):
+        dphi, cap = dec.estimator([T, T], _flat(xs), _flat(mus), _flat(conds), spks, 0.0, capture_block=blk,
+                                  want_input_embed=True, want_norm_out=True)
+        got_blk = cap["block"].reshape(2, T, 1024)
+        assert rel_max(got_blk, g[f"dit_block{blk}"]) < STAGE_TOL, blk
+    assert rel_max(cap["input_embed"].reshape(2, T, 1024), g["dit_input_embed_step1"]) < STAGE_TOL
+    assert rel_max(cap["norm_out"].reshape(2, T, 1024), g["dit_norm_out_step1"]) < STAGE_TOL
+    d = np.stack(_split(dphi, [T, T]))
+    assert rel_max(d, g["dphi_step1"]) < STAGE_TOL
+
+
+def test_estimator_vs_oracle_long(dec, weights):
+    """Random inputs, T = 300 and 129 (several 128-row tiles, ragged tail)."""
+    rng = np.random.default_rng(5)
+    L = [300, 129]
+    xs = [rng.standard_normal((80, n)).astype(np.float32) for n in L]
+    mus = [rng.standard_normal((80, n)).astype(np.float32) for n in L]
+    conds = [np.where(np.arange(n) < n // 5, rng.standard_normal((80, n)), 0).astype(np.float32) for n in L]
+    spks = rng.standard_normal((2, 80)).astype(np.float32)
+    dphi, _ = dec.estimator(L, _flat(xs), _flat(mus), _flat(conds), spks, 0.42)
+    got = _split(dphi, L)
+    for i, n in enumerate(L):
+        ref = fo.dit_forward(weights, xs[i][None], mus[i][None], np.array([0.42], np.float32), spks[i:i + 1],
+                             conds[i][None])[0]
+        assert rel_max(got[i], ref) < STAGE_TOL
+        assert rel_l2(got[i], ref) < STAGE_TOL
+
+
+def test_estimator_block_causal(dec, weights):
+    g = golden("dit_chunk.npz")
+    L = [int(n) for n in g["lengths"]]
+    xs = [g["x"][b, :, :n] for b, n in enumerate(L)]
+    mus = [g["mu"][b, :, :n] for b, n in enumerate(L)]
+    conds = [g["cond"][b, :, :n] for b, n in enumerate(L)]
+    dphi, _ = dec.estimator(L, _flat(xs), _flat(mus), _flat(conds), g["spks"], float(g["t"]), chunk=int(g["chunk"]))
+    for b, d in enumerate(_split(dphi, L)):
+        assert rel_max(d, g["dphi"][b, :, :L[b]]) < STAGE_TOL
+
+
+def test_decode_padded_batch_golden(dec):
+    """Key-padding batch (lengths 20, 32): 10-step CFG solve vs the golden."""
+    g = golden("dit_padded.npz")
+    L = [int(n) for n in g["lengths"]]
+    out = dec.decode(L, [g["mu"][b, :, :n] for b, n in enumerate(L)], [g["cond"][b, :, :n] for b, n in enumerate(L)],
+                     g["spks"], noise=[g["x"][b, :, :n] for b, n in enumerate(L)])
+    for b, m in enumerate(_split(out, L)):
+        ref = g["solve"][b, :, :L[b]]
+        assert np.abs(m - ref).max() < MEL_ABS_TOL
+
+
+def test_infer_fixture(dec):
+    """Token-level infer (frontend + 10-step decode) on the reference's own
+    24-frame validation case, stage captures included."""
+    g = golden("flow_fixture.npz")
+    dbg = {}
+    mel = dec.infer(g["prompt_tokens"][0], g["tokens"][0], g["prompt_feat"][0], g["spk_embedding"][0],
+                    noise_z=g["noise_z"][0], debug=dbg)
+    assert mel is not None
+    assert mel.shape == g["feat"][0].shape
+    assert np.abs(mel - g["feat"][0]).max() < MEL_ABS_TOL
+    assert rel_max(dbg["spk"], g["spk"][0]) < 1e-5
+    assert rel_max(dbg["mu"], g["mu"][0]) < 1e-5
+    assert rel_max(dbg["cond"], g["cond"][0]) < 1e-6
+    assert rel_max(dbg["time_embed"], g["time_embed_step1"][0]) < 1e-5
+    assert rel_max(dbg["input_embed"], g["dit_input_embed_step1"]) < STAGE_TOL
+    for i in (0, 10, 21):
+        assert rel_max(dbg["blocks"][i], g[f"dit_block{i}"]) < STAGE_TOL
+    assert rel_max(dbg["norm_out"], g["dit_norm_out_step1"]) < STAGE_TOL
+    assert rel_max(dbg["dphi"], g["dphi_step1"]) < STAGE_TOL
+
+
+def test_decode_chunked_vs_oracle(dec, weights):
+    """Block-causal (chunk 50) 10-step CFG decode of two streams vs the oracle."""
+    rng = np.random.default_rng(4)
+    L = [56, 106]
+    mus = [rng.standard_normal((80, n)).astype(np.float32) for n in L]
+    conds = [np.zeros((80, n), np.float32) for n in L]
+    noise = [rng.standard_normal((80, n)).astype(np.float32) for n in L]
+    spks = rng.standard_normal((2, 80)).astype(np.float32)
+    out = dec.decode(L, mus, conds, spks, noise=noise, chunk=50)
+    for b, n in enumerate(L):
+        ref = fo.solve_euler(weights, noise[b][None], mus[b][None], spks[b:b + 1], conds[b][None],
+                             fo.block_causal_mask([n], n, 50))[0]
+        assert np.abs(_split(out, L)[b] - ref).max() < MEL_ABS_TOL
+
+
+def test_errors_are_reported(dec, tmp_path):
+    """Bad inputs fail with a status, not a crash."""
+    from larynx_b200 import FlowDecoder
+    d = FlowDecoder(0)
+    assert not d.load(str(tmp_path / "missing.gguf"))
+    bad = tmp_path / "bad.gguf"
+    bad.write_bytes(b"GGUF" + b"\0" * 64)
+    assert not d.load(str(bad))
+    assert "infer" and d.infer([1], [2], np.zeros((0, 80)), np.ones(192)) is None  # not loaded
+    d.close()
+    with pytest.raises(Exception):
+        dec.decode([0], np.zeros(0), np.zeros(0), np.zeros((1, 80)), noise=np.zeros(0))
