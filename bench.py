@@ -1,0 +1,409 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 Flow decoder hot path.
+
+Workload (the configuration the metric is quoted on at
+1/2/4/8 GPUs): per GPU, 64 independent utterances with lengths uniform in
+[100, 1500] mel frames (seed 3), each with its own N(0,1) mu/spks/noise and a
+prompt cond over its first 20% of frames, decoded by the 10-step cosine CFM
+Euler solver with CFG pairing (batch 2 per utterance) through the 22-block
+DiT, key-padding semantics (utterances packed without padding).  Weights are
+seeded random N(0, 0.02) of the real architecture (no checkpoint offline).
+
+One step = one full 10-step CFG decode of the rank's 64-utterance batch.
+`value` = mel frames decoded by all ranks / max-over-ranks device time, with
+inputs resident in HBM (lx_flow_decode_device); `e2e` = the same through the
+host-buffer C-ABI call lx_flow_decode (pinned inputs, H2D + compute + D2H of
+the mel every step).  Weak scaling: every rank decodes its own batch; there is
+no collective on the data path (barriers and the timing max only).
+
+`--impl reference` times the reference's CPU path on the host cores.  The
+reference's own CPU engine (GGML, LARYNX_BACKEND=cpu) cannot be built (ggml is
+an un-vendored submodule), so the numpy restatement of the reference's Flow
+model (oracle/, checked against the reference's golden vectors) runs in its
+place, on a bounded sample of the workload per step.
+"""
+
+import argparse
+import datetime
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC = "Flow mel-frames/s (10-step CFG)"
+UNIT = "mel-frames/s"
+N_UTT = 64
+REF_SAMPLE_T = 200
+
+
+def cfg3_lengths(n=N_UTT):
+    return np.random.default_rng(3).integers(100, 1501, n).astype(np.int32)
+
+
+def cfg3_inputs(lengths, seed):
+    rng = np.random.default_rng(seed)
+    tot = int(np.sum(lengths))
+    mu = rng.standard_normal(tot * 80, dtype=np.float32)
+    noise = rng.standard_normal(tot * 80, dtype=np.float32)
+    spks = rng.standard_normal((len(lengths), 80), dtype=np.float32)
+    cond = np.zeros(tot * 80, np.float32)
+    off = 0
+    for L in lengths:
+        L = int(L)
+        blk = cond[off:off + 80 * L].reshape(80, L)
+        p = int(0.2 * L)
+        blk[:, :p] = rng.standard_normal((80, p), dtype=np.float32)
+        off += 80 * L
+    return mu, cond, spks, noise
+
+
+def config_block(n_gpus, lengths):
+    return {"workload": f"cfg3: {len(lengths)} utterances per GPU, T~U[100,1500] frames (seed 3), "
+                        "10-step cosine CFM Euler, CFG batch 2, key-padding (packed varlen), dim 1024 x 22 blocks",
+            "model": "CosyVoice3 Flow DiT (22 blocks, dim 1024, 16 heads x 64, FF 2048)",
+            "global_batch": int(len(lengths) * n_gpus), "seq_len": "100-1500 frames",
+            "frames_per_gpu": int(np.sum(lengths)),
+            "parallelism": f"dp{n_gpus} (independent utterance batches, no collectives)",
+            "l2": "inputs larger than L2 (bf16 weights 378 MB + >1 GB activations per step)"}
+
+
+# ---------------------------------------------------------------------------
+# clocks sampling (nvidia-smi during the timed region)
+# ---------------------------------------------------------------------------
+class Clocks:
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self):
+        self.proc = None
+        self.f = None
+
+    def start(self):
+        try:
+            self.f = tempfile.TemporaryFile(mode="w+")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(5)
+        except Exception:
+            self.proc.kill()
+        self.f.seek(0)
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.f.read().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = max(mx, float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return None
+        busy = [v for v in sm if v > 0.5 * mx] or sm
+        return {"sm_mhz": float(np.median(busy)), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# roofline bookkeeping
+# ---------------------------------------------------------------------------
+def algorithmic_per_launch(cls, lengths):
+    """(quantity, unit, bound) per launch of a kernel class for the batch."""
+    tok = 2 * int(np.sum(lengths))           # CFG rows
+    sq = 2 * float(np.sum(np.asarray(lengths, np.float64) ** 2))
+    D, F, M = 1024, 2048, 80
+    flops = {"qkv_gemm": 2.0 * tok * 3 * D * D, "out_gemm": 2.0 * tok * D * D, "ff1_gemm": 2.0 * tok * F * D,
+             "ff2_gemm": 2.0 * tok * D * F, "attention": 4.0 * D * sq, "in_proj": 2.0 * tok * D * M,
+             "conv_pos": 2.0 * tok * D * 64 * 31, "proj_out_gemm": 2.0 * tok * M * D}
+    if cls in flops:
+        return flops[cls], "TFLOP/s", "tensor"
+    if cls == "adaln":
+        return tok * D * (4 + 2) + 2 * D * 4, "GB/s", "hbm"
+    if cls == "euler":
+        return int(np.sum(lengths)) * M * (4 * 4 + 2 * 2), "GB/s", "hbm"
+    return None, None, None
+
+
+def load_peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return {"hbm": float(d["hbm_gbs"]), "tensor": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
+                "src": "measured (MEASURED_PEAKS.json; sustained bf16 for kernels inside the long step)"}
+    return {"hbm": 6650.0, "tensor": 1400.0, "src": "fallback (6.65 TB/s, 1.4 PF/s sustained)"}
+
+
+def load_traffic():
+    p = os.path.join(REPO, "profiles", "traffic.json")
+    if os.path.exists(p):
+        try:
+            return json.load(open(p))
+        except Exception:
+            return {}
+    return {}
+
+
+# ---------------------------------------------------------------------------
+# CPU arms (the reference's algorithm restated in numpy: oracle/)
+# ---------------------------------------------------------------------------
+def cpu_sample_decode(W, T, seed):
+    from oracle import flow_oracle as fo
+    rng = np.random.default_rng(seed)
+    mu = rng.standard_normal((1, 80, T), dtype=np.float32)
+    z = rng.standard_normal((1, 80, T), dtype=np.float32)
+    spk = rng.standard_normal((1, 80), dtype=np.float32)
+    cond = np.zeros((1, 80, T), np.float32)
+    cond[:, :, :int(0.2 * T)] = rng.standard_normal((1, 80, int(0.2 * T)), dtype=np.float32)
+    t0 = time.perf_counter()
+    fo.solve_euler(W, z, mu, spk, cond)
+    return time.perf_counter() - t0
+
+
+def cpu_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def run_reference(args):
+    """The reference arm: rank 0 only; other ranks exit without work."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    from oracle import flow_oracle as fo
+    W = fo.synth_weights(seed=0, std=0.02)
+    for i in range(args.warmup):
+        cpu_sample_decode(W, REF_SAMPLE_T, 100 + i)
+    times = [cpu_sample_decode(W, REF_SAMPLE_T, 1000 + i) for i in range(args.steps)]
+    tot = float(np.sum(times))
+    value = args.steps * REF_SAMPLE_T / tot
+    sample = (f"1 utterance x {REF_SAMPLE_T} frames per step (cfg3 input distribution), full 10-step CFG decode, "
+              "numpy fp32 restatement of the reference's Flow model (oracle/); the reference's GGML CPU engine "
+              "is unavailable (ggml submodule not vendored)")
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": tot / args.steps * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": config_block(args.gpus, cfg3_lengths()),
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cpu_cores(), "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist_on = world > 1
+    if dist_on:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+
+    def barrier():
+        if dist_on:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v):
+        if not dist_on:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    from larynx_b200 import FlowDecoder
+    from larynx_b200.weights import write_synthetic_gguf
+
+    wdir = os.environ.get("LX_BENCH_DIR", tempfile.gettempdir())
+    gguf = os.path.join(wdir, "lx_bench_flow_synth.gguf")
+    if rank == 0 and not os.path.exists(gguf):
+        write_synthetic_gguf(gguf + ".tmp", seed=0, std=0.02)
+        os.replace(gguf + ".tmp", gguf)
+    barrier()
+    dec = FlowDecoder(local)
+    if not dec.load(gguf):
+        raise SystemExit(f"load failed: {dec.last_error}")
+
+    lengths = cfg3_lengths(args.utts)
+    tot = int(lengths.sum())
+    mu, cond, spks, noise = cfg3_inputs(lengths, seed=3000 + rank)
+    dev = torch.device("cuda", local)
+    d_mu = torch.from_numpy(mu).to(dev)
+    d_cond = torch.from_numpy(cond).to(dev)
+    d_spk = torch.from_numpy(spks).to(dev)
+    d_noise = torch.from_numpy(noise).to(dev)
+    d_out = torch.empty_like(d_mu)
+    stream = torch.cuda.Stream(device=dev)
+
+    def step():
+        dec.decode_device(lengths, d_mu.data_ptr(), d_cond.data_ptr(), d_spk.data_ptr(), d_noise.data_ptr(),
+                          d_out.data_ptr(), stream=stream.cuda_stream)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step()
+        stream.synchronize()
+        clocks = Clocks()
+        if rank == 0:
+            clocks.start()
+        barrier()
+        n0 = dec.launch_count
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        stream.synchronize()
+        barrier()
+        launches = dec.launch_count - n0
+        clk = clocks.stop() if rank == 0 else None
+        ms = max_over_ranks(e0.elapsed_time(e1))
+    finite = bool(torch.isfinite(d_out).all().item())
+
+    # e2e through the host-buffer C-ABI call, pinned inputs and output
+    e2e = None
+    if not args.no_e2e:
+        pin = lambda a: torch.from_numpy(a).pin_memory()
+        p_mu, p_cond, p_spk, p_noise = pin(mu), pin(cond), pin(spks), pin(noise)
+        p_out = torch.empty(tot * 80, dtype=torch.float32).pin_memory()
+        args_np = (p_mu.numpy(), p_cond.numpy(), p_spk.numpy(), p_noise.numpy(), p_out.numpy())
+
+        def e2e_step():
+            dec.decode(lengths, args_np[0], args_np[1], args_np[2], noise=args_np[3], out=args_np[4])
+
+        for _ in range(max(1, min(args.warmup, 2))):
+            e2e_step()
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            e2e_step()
+        barrier()
+        e2e_s = max_over_ranks(time.perf_counter() - t0)
+        e2e = {"value": world * tot * args.steps / e2e_s, "unit": UNIT,
+               "h2d_bytes_per_step": int(mu.nbytes + cond.nbytes + spks.nbytes + noise.nbytes),
+               "d2h_bytes_per_step": int(tot * 80 * 4), "ms_per_step": e2e_s / args.steps * 1e3,
+               "api": "lx_flow_decode (host buffers)"}
+
+    # per-kernel-class device times (CUDA events around every launch, no graph)
+    with torch.cuda.stream(stream):
+        prof = dec.profile_decode(lengths, d_mu.data_ptr(), d_cond.data_ptr(), d_spk.data_ptr(), d_noise.data_ptr(),
+                                  d_out.data_ptr(), stream=stream.cuda_stream)
+    peaks = load_peaks()
+    traffic = load_traffic()
+    dom = max(prof, key=lambda k: prof[k][0])
+    q, unit, bound = algorithmic_per_launch(dom, lengths)
+    dom_ms = prof[dom][0] / max(1, prof[dom][1])
+    achieved = (q / (dom_ms * 1e-3)) / (1e12 if unit == "TFLOP/s" else 1e9)
+    peak = peaks[bound]
+    roofline = {"kernel": dom, "bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
+                "frac": achieved / peak, "traffic": traffic.get(dom, {}).get("bytes_per_launch_scaled"),
+                "launch_ms": dom_ms, "launches_per_step": prof[dom][1],
+                "peak_source": peaks["src"], "note": "frac of measured peak"}
+    breakdown = {}
+    for k, (t, n) in prof.items():
+        if n == 0:
+            continue
+        qq, u, b = algorithmic_per_launch(k, lengths)
+        e = {"ms_total": round(t, 3), "launches": n, "share": round(t / sum(v[0] for v in prof.values()), 4)}
+        if qq:
+            a = (qq / (t / n * 1e-3)) / (1e12 if u == "TFLOP/s" else 1e9)
+            e.update({"achieved": round(a, 1), "unit": u, "frac_of_peak": round(a / peaks[b], 3)})
+        breakdown[k] = e
+
+    # single long utterance latency on this GPU
+    extra = {}
+    if not args.no_cfg2:
+        L2 = np.array([1000], np.int32)
+        m2, c2, s2, n2 = cfg3_inputs(L2, seed=2)
+        t2 = [torch.from_numpy(a).to(dev) for a in (m2, c2, s2, n2)]
+        o2 = torch.empty_like(t2[0])
+        times = []
+        with torch.cuda.stream(stream):
+            for i in range(8):
+                a0 = torch.cuda.Event(enable_timing=True)
+                a1 = torch.cuda.Event(enable_timing=True)
+                a0.record(stream)
+                dec.decode_device(L2, t2[0].data_ptr(), t2[1].data_ptr(), t2[2].data_ptr(), t2[3].data_ptr(),
+                                  o2.data_ptr(), stream=stream.cuda_stream)
+                a1.record(stream)
+                stream.synchronize()
+                if i >= 3:
+                    times.append(a0.elapsed_time(a1))
+        extra["cfg2_T1000_latency_ms"] = float(np.median(times))
+        extra["cfg2_frames_per_s"] = 1000.0 / (float(np.median(times)) * 1e-3)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        from oracle import flow_oracle as fo
+        W = fo.synth_weights(seed=0, std=0.02)
+        cpu_sample_decode(W, 48, 7)  # warm the BLAS threads
+        ts = [cpu_sample_decode(W, REF_SAMPLE_T, 1000 + i) for i in range(2)]
+        cpu = {"value": REF_SAMPLE_T * len(ts) / float(np.sum(ts)), "unit": UNIT, "cores": cpu_cores(),
+               "kind": "port",
+               "sample": f"1 utterance x {REF_SAMPLE_T} frames (cfg3 input distribution), 10-step CFG decode, "
+                         f"x{len(ts)}; numpy fp32 restatement of the reference's Flow model (oracle/)"}
+
+    if rank == 0:
+        value = world * tot * args.steps / (ms * 1e-3)
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random weights and inputs)",
+                "config": config_block(world, lengths), "rtf": (ms / args.steps * 1e-3) / (tot / 50.0),
+                "e2e": e2e, "gpu_launches": int(launches), "roofline": roofline, "cpu_baseline": cpu,
+                "clocks": clk, "kernels": breakdown, "finite": finite, **extra}
+        print(json.dumps(line), flush=True)
+    dec.close()
+    if dist_on:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--utts", type=int, default=N_UTT)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-cfg2", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -137,6 +137,16 @@ int lx_flow_estimator(lx_flow* h, int n_seq, const int32_t* lengths, const float
                       const float* cond, const float* spks, float t, int chunk, float* dphi_out,
                       float* input_embed_out, float* block_out, int block_index, float* norm_out);
 
+/* Diagnostic: runs lx_flow_decode_device without CUDA graphs, bracketing
+ * every kernel with CUDA events on the launch stream, and returns per kernel
+ * class the summed device milliseconds and launch counts (synchronous).
+ * Classes (n_class >= 11): 0 input projection, 1 conv-pos, 2 AdaLN-mod,
+ * 3 QKV GEMM, 4 attention, 5 out GEMM, 6 FF1 GEMM, 7 FF2 GEMM, 8 proj_out GEMM,
+ * 9 Euler/CFG update, 10 other.  No reference counterpart (the reference has
+ * no timers, per its own docs). */
+int lx_flow_profile_decode(lx_flow* h, const lx_flow_batch* b, void* stream, double* ms_by_class,
+                           int* launches_by_class, int n_class);
+
 /* Total number of kernel launches enqueued by this handle so far. */
 uint64_t lx_flow_launch_count(const lx_flow* h);
 

@@ -83,6 +83,32 @@ struct lx_flow {
   };
   std::map<std::string, GraphEntry> graphs;
   bool use_graphs = true;
+  // per-kernel-class CUDA-event timing (lx_flow_profile_decode)
+  struct ProfRec {
+    int cls;
+    cudaEvent_t a, b;
+  };
+  struct Prof {
+    std::vector<cudaEvent_t> pool;
+    size_t used = 0;
+    std::vector<ProfRec> recs;
+    cudaEvent_t get() {
+      if (used == pool.size()) {
+        cudaEvent_t e;
+        cudaEventCreate(&e);
+        pool.push_back(e);
+      }
+      return pool[used++];
+    }
+    ~Prof() {
+      for (auto e : pool) cudaEventDestroy(e);
+    }
+  };
+  Prof* prof = nullptr;
+  // last plan uploaded to the workspace (skips rebuilding an identical layout)
+  Plan cached_plan;
+  uint64_t cached_gen = 0;
+  bool cached_valid = false;
   // frontend scratch
   float *f_spk_in = nullptr, *f_spk = nullptr, *f_emb = nullptr, *f_h = nullptr, *f_pre = nullptr,
         *f_mu = nullptr, *f_cond = nullptr, *f_pf = nullptr;
@@ -96,6 +122,27 @@ struct lx_flow {
 };
 
 namespace {
+
+// kernel classes reported by lx_flow_profile_decode
+enum KClass : int {
+  K_INPROJ = 0, K_CONV = 1, K_ADALN = 2, K_QKV = 3, K_ATTN = 4, K_OUT = 5, K_FF1 = 6, K_FF2 = 7,
+  K_PROJOUT = 8, K_EULER = 9, K_OTHER = 10, K_NCLASS = 11
+};
+
+// Bracket one launch with events when profiling (never inside a graph capture).
+template <class F>
+inline void timed(lx_flow* h, int cls, cudaStream_t s, F&& launch) {
+  if (h->prof) {
+    cudaEvent_t a = h->prof->get();
+    cudaEventRecord(a, s);
+    launch();
+    cudaEvent_t b = h->prof->get();
+    cudaEventRecord(b, s);
+    h->prof->recs.push_back({cls, a, b});
+  } else {
+    launch();
+  }
+}
 
 int cuda_fail(lx_flow* h, cudaError_t e, const char* what) {
   return h->fail(e == cudaErrorMemoryAllocation ? LX_ERR_OOM : LX_ERR_CUDA,
@@ -346,6 +393,7 @@ int load_model(lx_flow* h, const char* path) {
 // --------------------------------------------------------------------------
 // batch plan
 // --------------------------------------------------------------------------
+std::string plan_key(int n_utt, const int32_t* lengths, bool cfg_pairs, int chunk, int steps);
 // cfg_pairs: every utterance contributes a conditional and a CFG-zeroed
 // sequence (decode); otherwise each input is one sequence (estimator).
 Plan make_plan(int n_utt, const int32_t* lengths, bool cfg_pairs, int chunk, int steps) {
@@ -398,8 +446,7 @@ Plan make_plan(int n_utt, const int32_t* lengths, bool cfg_pairs, int chunk, int
   }
   for (int s = 0; s < p.n_seq; ++s)
     for (int q0 = 0; q0 < p.seq_len[s]; q0 += 128) p.tiles.push_back(AttnTile{p.seq_start[s], p.seq_len[s], q0, 0});
-  p.key = std::string(cfg_pairs ? "D" : "E") + ":" + std::to_string(chunk) + ":" + std::to_string(steps) + ":";
-  for (int u = 0; u < n_utt; ++u) p.key += std::to_string(lengths[u]) + ",";
+  p.key = plan_key(n_utt, lengths, cfg_pairs, chunk, steps);
   return p;
 }
 
@@ -476,6 +523,7 @@ int ensure_workspace(lx_flow* h, const Plan& p, size_t in_floats, int n_utt) {
 
 int upload_plan(lx_flow* h, const Plan& p, cudaStream_t s) {
   Workspace& w = h->ws;
+  h->cached_valid = false;
   CK(cudaMemcpyAsync(w.pos, p.pos.data(), p.R * sizeof(int), cudaMemcpyHostToDevice, s));
   CK(cudaMemcpyAsync(w.p2s, p.p2s.data(), p.R * sizeof(int), cudaMemcpyHostToDevice, s));
   CK(cudaMemcpyAsync(w.s2p, p.s2p.data(), p.Rs * sizeof(int), cudaMemcpyHostToDevice, s));
@@ -533,26 +581,35 @@ void enqueue_dit(lx_flow* h, const Plan& p, const float* mod, const float* mod_f
   const int bn1024 = pick_bn(R, DIM), bnq = pick_bn(R, QKV_N), bnf = pick_bn(R, FF);
   const int i1024 = bn1024 == 256, iq = bnq == 256, iff = bnf == 256;
   int* err = h->d_err;
-  gemm_in_proj(bn1024, w.tm_xb, W.tm_winx[i1024], R, w.cst, w.x, w.stage1, w.p2s, err, s);
-  conv_pos(w.tm_stage1, W.tm_wconv[0], p.Rs, W.bconv[0], 0, w.stage2, w.x, w.s2p, err, s);
-  conv_pos(w.tm_stage2, W.tm_wconv[1], p.Rs, W.bconv[1], 1, nullptr, w.x, w.s2p, err, s);
+  timed(h, K_INPROJ, s, [&] { gemm_in_proj(bn1024, w.tm_xb, W.tm_winx[i1024], R, w.cst, w.x, w.stage1, w.p2s, err, s); });
+  timed(h, K_CONV, s, [&] { conv_pos(w.tm_stage1, W.tm_wconv[0], p.Rs, W.bconv[0], 0, w.stage2, w.x, w.s2p, err, s); });
+  timed(h, K_CONV, s, [&] { conv_pos(w.tm_stage2, W.tm_wconv[1], p.Rs, W.bconv[1], 1, nullptr, w.x, w.s2p, err, s); });
   h->launches += 3;
   if (cap && cap->input_embed) {
     gather_rows(cap->input_embed, w.x, w.seq_rows, p.F, DIM, s);
     ++h->launches;
   }
   for (int l = 0; l < DEPTH; ++l) {
-    const float* m = mod + static_cast<size_t>(l) * MOD_N;  // shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp
-    adaln_rows(w.x, w.xn, m + 0 * DIM, m + 1 * DIM, R, s);
-    gemm_qkv(bnq, w.tm_xn, W.tm_wqkv[iq], R, l * QKV_N, W.bqkv + static_cast<size_t>(l) * QKV_N, w.q, w.k, w.vt,
-             w.Rv, w.pos, W.rope, err, s);
-    attention(w.tm_q, w.tm_k, w.tm_vt, w.tiles, static_cast<int>(p.tiles.size()), chunk, w.ao, err, s);
-    gemm_gate_res(bn1024, w.tm_ao, W.tm_wo[i1024], R, DIM, l * DIM, W.bo + static_cast<size_t>(l) * DIM, m + 2 * DIM,
-                  w.x, err, s);
-    adaln_rows(w.x, w.xn, m + 3 * DIM, m + 4 * DIM, R, s);
-    gemm_gelu(bnf, w.tm_xn, W.tm_w1[iff], R, l * FF, W.b1 + static_cast<size_t>(l) * FF, w.h, err, s);
-    gemm_gate_res(bn1024, w.tm_h, W.tm_w2[i1024], R, FF, l * DIM, W.b2 + static_cast<size_t>(l) * DIM, m + 5 * DIM,
-                  w.x, err, s);
+    // modulation chunks: shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp
+    const float* m = mod + static_cast<size_t>(l) * MOD_N;
+    timed(h, K_ADALN, s, [&] { adaln_rows(w.x, w.xn, m + 0 * DIM, m + 1 * DIM, R, s); });
+    timed(h, K_QKV, s, [&] {
+      gemm_qkv(bnq, w.tm_xn, W.tm_wqkv[iq], R, l * QKV_N, W.bqkv + static_cast<size_t>(l) * QKV_N, w.q, w.k, w.vt,
+               w.Rv, w.pos, W.rope, err, s);
+    });
+    timed(h, K_ATTN, s,
+          [&] { attention(w.tm_q, w.tm_k, w.tm_vt, w.tiles, static_cast<int>(p.tiles.size()), chunk, w.ao, err, s); });
+    timed(h, K_OUT, s, [&] {
+      gemm_gate_res(bn1024, w.tm_ao, W.tm_wo[i1024], R, DIM, l * DIM, W.bo + static_cast<size_t>(l) * DIM,
+                    m + 2 * DIM, w.x, err, s);
+    });
+    timed(h, K_ADALN, s, [&] { adaln_rows(w.x, w.xn, m + 3 * DIM, m + 4 * DIM, R, s); });
+    timed(h, K_FF1, s,
+          [&] { gemm_gelu(bnf, w.tm_xn, W.tm_w1[iff], R, l * FF, W.b1 + static_cast<size_t>(l) * FF, w.h, err, s); });
+    timed(h, K_FF2, s, [&] {
+      gemm_gate_res(bn1024, w.tm_h, W.tm_w2[i1024], R, FF, l * DIM, W.b2 + static_cast<size_t>(l) * DIM,
+                    m + 5 * DIM, w.x, err, s);
+    });
     h->launches += 7;
     if (cap && cap->block && cap->block_index == l) {
       gather_rows(cap->block, w.x, w.seq_rows, p.F, DIM, s);
@@ -564,8 +621,8 @@ void enqueue_dit(lx_flow* h, const Plan& p, const float* mod, const float* mod_f
     }
   }
   // AdaLayerNormZero_Final: chunk order scale, shift (flow_reference.py:192)
-  adaln_rows(w.x, w.xn, mod_final + DIM, mod_final, R, s);
-  gemm_f32(128, w.tm_xn, W.tm_wout, R, MEL, DIM, W.bout, w.dphi, MEL, err, s);
+  timed(h, K_ADALN, s, [&] { adaln_rows(w.x, w.xn, mod_final + DIM, mod_final, R, s); });
+  timed(h, K_PROJOUT, s, [&] { gemm_f32(128, w.tm_xn, W.tm_wout, R, MEL, DIM, W.bout, w.dphi, MEL, err, s); });
   h->launches += 2;
   if (cap && cap->norm_out) {
     gather_rows_bf16(cap->norm_out, w.xn, w.seq_rows, p.F, DIM, s);
@@ -578,7 +635,8 @@ void enqueue_decode_steps(lx_flow* h, const Plan& p, int steps, int chunk, cudaS
   for (int st = 0; st < steps; ++st) {
     enqueue_dit(h, p, W.mod + static_cast<size_t>(st) * DEPTH * MOD_N, W.mod_final + static_cast<size_t>(st) * 2 * DIM,
                 chunk, s, nullptr);
-    euler_update(h->ws.xs, h->ws.dphi, h->ws.frame_rows, h->ws.xb, p.F, W.sched_dt[st], CFG_RATE, s);
+    timed(h, K_EULER, s,
+          [&] { euler_update(h->ws.xs, h->ws.dphi, h->ws.frame_rows, h->ws.xb, p.F, W.sched_dt[st], CFG_RATE, s); });
     ++h->launches;
   }
 }
@@ -616,17 +674,30 @@ int validate_batch(lx_flow* h, const lx_flow_batch* b, size_t* total) {
   return LX_OK;
 }
 
+std::string plan_key(int n_utt, const int32_t* lengths, bool cfg_pairs, int chunk, int steps) {
+  std::string k = std::string(cfg_pairs ? "D" : "E") + ":" + std::to_string(chunk) + ":" + std::to_string(steps) + ":";
+  for (int u = 0; u < n_utt; ++u) k += std::to_string(lengths[u]) + ",";
+  return k;
+}
+
 // decode with inputs already on the device
 int run_decode(lx_flow* h, const lx_flow_batch* b, const float* mu, const float* cond, const float* spks,
                const float* noise, float* out, cudaStream_t s) {
   const int steps = b->n_steps == 0 ? h->W.n_sched : b->n_steps;
-  Plan p = make_plan(b->n_utt, b->lengths, true, b->chunk, steps);
-  int rc = ensure_workspace(h, p, static_cast<size_t>(p.F) * MEL, b->n_utt);
-  if (rc) return rc;
-  if ((rc = upload_plan(h, p, s))) return rc;
+  int rc;
+  const std::string key = plan_key(b->n_utt, b->lengths, true, b->chunk, steps);
+  if (!(h->cached_valid && h->cached_plan.key == key && h->cached_gen == h->ws.generation)) {
+    Plan np_ = make_plan(b->n_utt, b->lengths, true, b->chunk, steps);
+    if ((rc = ensure_workspace(h, np_, static_cast<size_t>(np_.F) * MEL, b->n_utt))) return rc;
+    if ((rc = upload_plan(h, np_, s))) return rc;
+    h->cached_plan = std::move(np_);
+    h->cached_gen = h->ws.generation;
+    h->cached_valid = true;
+  }
+  const Plan& p = h->cached_plan;
   StepIO io{mu, cond, spks, noise, out};
   enqueue_setup(h, p, io, s);
-  if (h->use_graphs) {
+  if (h->use_graphs && !h->prof) {
     char ptrs[64];
     std::snprintf(ptrs, sizeof ptrs, "|g%llu", static_cast<unsigned long long>(h->ws.generation));
     const std::string key = p.key + ptrs;
@@ -764,6 +835,35 @@ int lx_flow_decode_device(lx_flow* h, const lx_flow_batch* b, void* stream) {
   CK(cudaSetDevice(h->device));
   cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : h->stream;
   return run_decode(h, b, b->mu, b->cond, b->spks, b->noise, b->mel_out, s);
+}
+
+int lx_flow_profile_decode(lx_flow* h, const lx_flow_batch* b, void* stream, double* ms_by_class,
+                           int* launches_by_class, int n_class) {
+  if (!h || !ms_by_class || !launches_by_class || n_class < K_NCLASS) return LX_ERR_ARG;
+  if (!h->loaded) return h->fail(LX_ERR_STATE, "lx_flow_load_gguf has not succeeded");
+  size_t tot = 0;
+  int rc = validate_batch(h, b, &tot);
+  if (rc) return rc;
+  if (!b->noise) return h->fail(LX_ERR_ARG, "lx_flow_profile_decode needs explicit device noise");
+  CK(cudaSetDevice(h->device));
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : h->stream;
+  lx_flow::Prof prof;
+  h->prof = &prof;
+  rc = run_decode(h, b, b->mu, b->cond, b->spks, b->noise, b->mel_out, s);
+  h->prof = nullptr;
+  if (rc) return rc;
+  if ((rc = check_device_error(h, s))) return rc;
+  for (int c = 0; c < n_class; ++c) {
+    ms_by_class[c] = 0.0;
+    launches_by_class[c] = 0;
+  }
+  for (auto& r : prof.recs) {
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, r.a, r.b);
+    ms_by_class[r.cls] += ms;
+    launches_by_class[r.cls] += 1;
+  }
+  return LX_OK;
 }
 
 int lx_flow_decode(lx_flow* h, const lx_flow_batch* b) {
@@ -966,6 +1066,7 @@ int lx_flow_infer(lx_flow* h, const int32_t* prompt_tokens, int n_prompt, const 
       crow[T + t] = p.seq_start[1] + t;
     }
     CK(cudaMemcpyAsync(w.seq_rows, crow.data(), rows2 * sizeof(int), cudaMemcpyHostToDevice, s));
+    h->cached_valid = false;
     Plan pc = p;
     pc.F = static_cast<int>(rows2);
     if (debug->input_proj) {

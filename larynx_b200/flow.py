@@ -30,7 +30,11 @@ ERRORS = {1: "LX_ERR_ARG", 2: "LX_ERR_IO", 3: "LX_ERR_FORMAT", 4: "LX_ERR_SHAPE"
 # Symbols declared in include/larynx_flow.h
 EXPORTS = ("lx_flow_create", "lx_flow_destroy", "lx_flow_last_error", "lx_flow_load_gguf", "lx_flow_load_noise",
            "lx_flow_infer", "lx_flow_decode", "lx_flow_decode_device", "lx_flow_estimator",
-           "lx_flow_launch_count", "lx_flow_op", "lx_flow_op_gemm", "lx_flow_op_attention")
+           "lx_flow_launch_count", "lx_flow_op", "lx_flow_op_gemm", "lx_flow_op_attention",
+           "lx_flow_profile_decode")
+
+KERNEL_CLASSES = ("in_proj", "conv_pos", "adaln", "qkv_gemm", "attention", "out_gemm", "ff1_gemm", "ff2_gemm",
+                  "proj_out_gemm", "euler", "other")
 
 _f32p = ctypes.POINTER(ctypes.c_float)
 _i32p = ctypes.POINTER(ctypes.c_int32)
@@ -76,6 +80,9 @@ def load_library(path: str = LIB_PATH):
     lib.lx_flow_launch_count.argtypes = [vp]
     lib.lx_flow_launch_count.restype = ctypes.c_uint64
     lib.lx_flow_op.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, vp, vp, _f32p, _f32p, _f32p, _i32p, vp]
+    lib.lx_flow_profile_decode.argtypes = [vp, ctypes.POINTER(LxFlowBatch), vp, ctypes.POINTER(ctypes.c_double),
+                                           ctypes.POINTER(ctypes.c_int), ctypes.c_int]
+    lib.lx_flow_profile_decode.restype = ctypes.c_int
     lib.lx_flow_op_gemm.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, vp, vp, vp, vp, vp]
     lib.lx_flow_op_attention.argtypes = [ctypes.c_int, _i32p, vp, vp, vp, vp, ctypes.c_int, vp]
     for name in ("lx_flow_op_gemm", "lx_flow_op_attention", "lx_flow_create", "lx_flow_load_gguf", "lx_flow_load_noise", "lx_flow_infer", "lx_flow_decode",
@@ -179,17 +186,24 @@ class FlowDecoder:
 
     # --- extensions ----------------------------------------------------
     def decode(self, lengths: Sequence[int], mu, cond, spks, noise=None, chunk: int = 0,
-               n_steps: int = 0) -> np.ndarray:
+               n_steps: int = 0, out: Optional[np.ndarray] = None) -> np.ndarray:
         """Batched 10-step CFG decode.  mu/cond/noise: concatenation of the
         utterances' [80, T_u] blocks (flat or a list of arrays); spks [U, 80].
-        Returns the flat concatenation of the final [80, T_u] blocks."""
+        Returns the flat concatenation of the final [80, T_u] blocks (written
+        into ``out`` when given: float32, contiguous, sum(T_u) * 80)."""
         L = np.ascontiguousarray(np.asarray(lengths, dtype=np.int32))
         cat = lambda a: _f32(np.concatenate([np.asarray(x, np.float32).reshape(-1) for x in a])
                              if isinstance(a, (list, tuple)) else np.asarray(a, np.float32).reshape(-1))
         mu_, cond_ = cat(mu), cat(cond)
         nz = None if noise is None else cat(noise)
         sp = _f32(spks).reshape(-1)
-        out = np.empty(int(L.sum()) * 80, np.float32)
+        n = int(L.sum()) * 80
+        if out is None:
+            out = np.empty(n, np.float32)
+        elif out.dtype != np.float32 or out.size != n or not out.flags["C_CONTIGUOUS"]:
+            raise ValueError("out must be a contiguous float32 array of sum(lengths) * 80 elements")
+        if mu_.size != n or cond_.size != n or (nz is not None and nz.size != n) or sp.size != 80 * L.size:
+            raise ValueError("input sizes do not match the lengths")
         b = LxFlowBatch(int(L.size), L.ctypes.data_as(_i32p), mu_.ctypes.data, cond_.ctypes.data, sp.ctypes.data,
                         None if nz is None else nz.ctypes.data, out.ctypes.data, int(chunk), int(n_steps))
         self._raise(self._lib.lx_flow_decode(self._h, ctypes.byref(b)), "decode")
@@ -204,6 +218,20 @@ class FlowDecoder:
                         int(chunk), 0)
         self._raise(self._lib.lx_flow_decode_device(self._h, ctypes.byref(b), ctypes.c_void_p(stream or None)),
                     "decode_device")
+
+    def profile_decode(self, lengths, mu_ptr: int, cond_ptr: int, spks_ptr: int, noise_ptr: int, out_ptr: int,
+                       chunk: int = 0, stream: int = 0) -> dict:
+        """Device-pointer decode without graphs, every kernel bracketed by CUDA
+        events; returns {class: (total_ms, launches)}."""
+        L = np.ascontiguousarray(np.asarray(lengths, dtype=np.int32))
+        b = LxFlowBatch(int(L.size), L.ctypes.data_as(_i32p), mu_ptr, cond_ptr, spks_ptr, noise_ptr, out_ptr,
+                        int(chunk), 0)
+        n = len(KERNEL_CLASSES)
+        ms = (ctypes.c_double * n)()
+        cnt = (ctypes.c_int * n)()
+        self._raise(self._lib.lx_flow_profile_decode(self._h, ctypes.byref(b), ctypes.c_void_p(stream or None), ms,
+                                                     cnt, n), "profile_decode")
+        return {k: (ms[i], cnt[i]) for i, k in enumerate(KERNEL_CLASSES)}
 
     def estimator(self, lengths: Sequence[int], x, mu, cond, spks, t: float, chunk: int = 0,
                   capture_block: Optional[int] = None, want_input_embed=False, want_norm_out=False):
