@@ -445,7 +445,8 @@ Plan make_plan(int n_utt, const int32_t* lengths, bool cfg_pairs, int chunk, int
     fo += L;
   }
   for (int s = 0; s < p.n_seq; ++s)
-    for (int q0 = 0; q0 < p.seq_len[s]; q0 += 128) p.tiles.push_back(AttnTile{p.seq_start[s], p.seq_len[s], q0, 0});
+    for (int q0 = 0; q0 < p.seq_len[s]; q0 += ATT_Q_ROWS)
+      p.tiles.push_back(AttnTile{p.seq_start[s], p.seq_len[s], q0, 0});
   p.key = plan_key(n_utt, lengths, cfg_pairs, chunk, steps);
   return p;
 }
@@ -515,6 +516,7 @@ int ensure_workspace(lx_flow* h, const Plan& p, size_t in_floats, int n_utt) {
     ok &= tmap_bf16(&w.tm_q, w.q, R, DIM, DIM, 128, 64);
     ok &= tmap_bf16(&w.tm_k, w.k, R, DIM, DIM, 128, 64);
     ok &= tmap_bf16(&w.tm_vt, w.vt, DIM, w.Rv, w.Rv, 64, 64);
+    ok &= tmap_f32(&w.tm_x, w.x, R, DIM, DIM, 128, 32);
     if (!ok) return h->fail(LX_ERR_CUDA, "cuTensorMapEncodeTiled failed for a workspace tensor");
     ++w.generation;
   }
@@ -600,15 +602,15 @@ void enqueue_dit(lx_flow* h, const Plan& p, const float* mod, const float* mod_f
     timed(h, K_ATTN, s,
           [&] { attention(w.tm_q, w.tm_k, w.tm_vt, w.tiles, static_cast<int>(p.tiles.size()), chunk, w.ao, err, s); });
     timed(h, K_OUT, s, [&] {
-      gemm_gate_res(bn1024, w.tm_ao, W.tm_wo[i1024], R, DIM, l * DIM, W.bo + static_cast<size_t>(l) * DIM,
-                    m + 2 * DIM, w.x, err, s);
+      gemm_gate_res_tma(w.tm_ao, W.tm_wo[0], w.tm_x, R, DIM, l * DIM, W.bo + static_cast<size_t>(l) * DIM,
+                        m + 2 * DIM, w.x, err, s);
     });
     timed(h, K_ADALN, s, [&] { adaln_rows(w.x, w.xn, m + 3 * DIM, m + 4 * DIM, R, s); });
     timed(h, K_FF1, s,
           [&] { gemm_gelu(bnf, w.tm_xn, W.tm_w1[iff], R, l * FF, W.b1 + static_cast<size_t>(l) * FF, w.h, err, s); });
     timed(h, K_FF2, s, [&] {
-      gemm_gate_res(bn1024, w.tm_h, W.tm_w2[i1024], R, FF, l * DIM, W.b2 + static_cast<size_t>(l) * DIM,
-                    m + 5 * DIM, w.x, err, s);
+      gemm_gate_res_tma(w.tm_h, W.tm_w2[0], w.tm_x, R, FF, l * DIM, W.b2 + static_cast<size_t>(l) * DIM,
+                        m + 5 * DIM, w.x, err, s);
     });
     h->launches += 7;
     if (cap && cap->block && cap->block_index == l) {

@@ -79,6 +79,7 @@ struct Workspace {
   size_t capCap = 0;
   int Rv = 0;
   CUtensorMap tm_xn, tm_ao, tm_h, tm_xb, tm_acond, tm_stage1, tm_stage2, tm_q, tm_k, tm_vt;
+  CUtensorMap tm_x;  // fp32 residual stream, box 128 x 32
   uint64_t generation = 0;
 };
 

@@ -41,6 +41,22 @@ static PFN_encodeTiled get_encode() {
   return fn;
 }
 
+bool tmap_f32(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows,
+              uint32_t box_cols) {
+  PFN_encodeTiled enc = get_encode();
+  if (!enc) return false;
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || (ld * 4) % 16 != 0) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld * 4};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   box_cols * 4 == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 bool tmap_bf16(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows,
                uint32_t box_cols) {
   PFN_encodeTiled enc = get_encode();
@@ -141,6 +157,30 @@ struct EpiGateRes {
   }
 };
 
+// x[row, col] = xin + gate[col] * (acc + bias[col]); xin is the residual tile
+// the loader warp staged in shared memory (MODE_RESID)
+struct EpiGateResSmem {
+  const float* bias;
+  const float* gate;
+  float* x;
+  __device__ __forceinline__ void operator()(int row, int col0, float (&v)[16], const float (&xin)[16]) const {
+    float4* xr = reinterpret_cast<float4*>(x + static_cast<size_t>(row) * DIM + col0);
+    const float4* b4 = reinterpret_cast<const float4*>(bias + col0);
+    const float4* g4 = reinterpret_cast<const float4*>(gate + col0);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float4 b = __ldg(b4 + j);
+      const float4 g = __ldg(g4 + j);
+      float4 o;
+      o.x = xin[4 * j + 0] + g.x * (v[4 * j + 0] + b.x);
+      o.y = xin[4 * j + 1] + g.y * (v[4 * j + 1] + b.y);
+      o.z = xin[4 * j + 2] + g.z * (v[4 * j + 2] + b.z);
+      o.w = xin[4 * j + 3] + g.w * (v[4 * j + 3] + b.w);
+      xr[j] = o;
+    }
+  }
+};
+
 struct EpiGelu {
   const float* bias;
   bf16* h;
@@ -220,8 +260,8 @@ struct EpiConv {
 // ---------------------------------------------------------------------------
 template <int BN, int STAGES, int MODE, class Epi>
 static void launch(const CUtensorMap& A, const CUtensorMap& B, int M, int N, int K, int b_off, const Epi& epi,
-                   int* err, cudaStream_t s) {
-  constexpr int smem = gemm_smem_bytes<BN, STAGES>();
+                   int* err, cudaStream_t s, const CUtensorMap* X = nullptr) {
+  constexpr int smem = gemm_smem_bytes<BN, STAGES, MODE>();
   static bool attr_done[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -234,7 +274,7 @@ static void launch(const CUtensorMap& A, const CUtensorMap& B, int M, int N, int
   if (tiles < grid) grid = tiles;
   if (grid <= 0) return;
   GemmShape sh{M, N, K, b_off, err};
-  k_gemm<BN, STAGES, MODE, Epi><<<grid, GEMM_THREADS, smem, s>>>(A, B, sh, epi);
+  k_gemm<BN, STAGES, MODE, Epi><<<grid, gemm_threads(MODE), smem, s>>>(A, B, X ? *X : A, sh, epi);
 }
 
 template <class Epi>
@@ -262,6 +302,12 @@ void gemm_gate_res(int bn, const CUtensorMap& A, const CUtensorMap& B, int M, in
                    const float* gate, float* x, int* err, cudaStream_t s) {
   EpiGateRes e{bias, gate, x};
   launch_bn(bn, A, B, M, DIM, K, b_off, e, err, s);
+}
+
+void gemm_gate_res_tma(const CUtensorMap& A, const CUtensorMap& B, const CUtensorMap& X, int M, int K, int b_off,
+                       const float* bias, const float* gate, float* x, int* err, cudaStream_t s) {
+  EpiGateResSmem e{bias, gate, x};
+  launch<128, 4, MODE_RESID>(A, B, M, DIM, K, b_off, e, err, s, &X);
 }
 
 void gemm_gelu(int bn, const CUtensorMap& A, const CUtensorMap& B, int M, int b_off, const float* bias, bf16* h,

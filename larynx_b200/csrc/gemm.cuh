@@ -12,6 +12,10 @@
 // The fp32 accumulator is double-buffered in tensor memory (2 x BN columns),
 // so the epilogue of tile i overlaps the MMAs of tile i+1.
 //
+// MODE_RESID adds a seventh warp that TMA-prefetches the fp32 residual tile
+// (128 x BN, as 32-column 128B-swizzled boxes) into shared memory while the
+// tile's MMAs run; the epilogue reads it from there instead of waiting on HBM.
+//
 // MODE_CONV turns the same pipeline into the causal grouped Conv1d of the
 // DiT's position embedding (k = 31, 16 groups of 64 channels): the K loop runs
 // over the 31 taps, the A box of tap k is the 128-row activation tile shifted
@@ -24,7 +28,7 @@
 
 namespace lx {
 
-enum GemmMode : int { MODE_GEMM = 0, MODE_CONV = 1 };
+enum GemmMode : int { MODE_GEMM = 0, MODE_CONV = 1, MODE_RESID = 2 };
 
 constexpr int GEMM_BM = 128;
 constexpr int GEMM_BK = 64;
@@ -41,18 +45,25 @@ __host__ __device__ constexpr int tmem_cols_for(int bn) {
   return (2 * bn) <= 32 ? 32 : (2 * bn) <= 64 ? 64 : (2 * bn) <= 128 ? 128 : (2 * bn) <= 256 ? 256 : 512;
 }
 
-template <int BN, int STAGES>
+__host__ __device__ constexpr int gemm_threads(int mode) { return mode == MODE_RESID ? 224 : GEMM_THREADS; }
+
+template <int BN, int STAGES, int MODE = MODE_GEMM>
 __host__ __device__ constexpr int gemm_smem_bytes() {
-  return 1024 /*alignment slack*/ + STAGES * (GEMM_BM * GEMM_BK * 2 + BN * GEMM_BK * 2) + 256 /*barriers*/;
+  return 1024 /*alignment slack*/ + STAGES * (GEMM_BM * GEMM_BK * 2 + BN * GEMM_BK * 2) +
+         (MODE == MODE_RESID ? GEMM_BM * BN * 4 : 0) + 256 /*barriers*/;
 }
 
 template <int BN, int STAGES, int MODE, class Epi>
-__global__ void __launch_bounds__(GEMM_THREADS, 1)
-    k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmShape sh,
-           Epi epi) {
+__global__ void __launch_bounds__(gemm_threads(MODE), 1)
+    k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+           const __grid_constant__ CUtensorMap tmX, GemmShape sh, Epi epi) {
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M=128 must be a multiple of 16 in [16,256]");
+  static_assert(MODE != MODE_RESID || BN % 32 == 0, "residual boxes are 32 columns wide");
+  constexpr bool RES = MODE == MODE_RESID;
   constexpr int A_BYTES = GEMM_BM * GEMM_BK * 2;
   constexpr int B_BYTES = BN * GEMM_BK * 2;
+  constexpr int X_BYTES = RES ? GEMM_BM * BN * 4 : 0;
+  constexpr int XBOX_BYTES = GEMM_BM * 32 * 4;  // 128 rows x 32 fp32 columns
   constexpr uint32_t TMEM_COLS = tmem_cols_for(BN);
   constexpr uint32_t IDESC = idesc_bf16_f32(GEMM_BM, BN);
 
@@ -60,11 +71,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint8_t* sX = sB + STAGES * B_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sX + X_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* x_full = tempty + 2;
+  uint64_t* x_empty = x_full + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(x_empty + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -79,12 +93,15 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       mbar_init(&tfull[a], 1);
       mbar_init(&tempty[a], 4);
     }
+    mbar_init(x_full, 1);
+    mbar_init(x_empty, 4);
     *abort_flag = 0;
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (RES) tma_prefetch_desc(&tmX);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, TMEM_COLS);
@@ -166,31 +183,68 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         if (acc == 0) acc_phase ^= 1u;
       }
     }
+  } else if (warp == 6) {
+    // residual loader (MODE_RESID only): the 128 x BN fp32 tile of the residual
+    if (RES && lane == 0) {
+      uint32_t xph = 0;
+      for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+        const int m0 = (tile / tiles_n) * GEMM_BM;
+        const int n0 = (tile % tiles_n) * BN;
+        if (!mbar_wait(x_empty, xph ^ 1u, sh.err, abort_flag, DEV_TIMEOUT_PRODUCER)) break;
+        mbar_arrive_expect_tx(x_full, X_BYTES);
+#pragma unroll
+        for (int b = 0; b < BN / 32; ++b) tma_load_2d(sX + b * XBOX_BYTES, &tmX, x_full, n0 + 32 * b, m0);
+        xph ^= 1u;
+      }
+    }
   } else {
     // epilogue warps 2..5 -> TMEM lane quarters 2,3,0,1
     const int q = warp & 3;
     int acc = 0;
     uint32_t acc_phase = 0;
+    uint32_t xph = 0;
     for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
       const int m0 = (tile / tiles_n) * GEMM_BM;
       const int n0 = (tile % tiles_n) * BN;
       bool ok = mbar_wait(&tfull[acc], acc_phase, sh.err, abort_flag, DEV_TIMEOUT_EPILOGUE);
+      if (RES && ok) ok = mbar_wait(x_full, xph, sh.err, abort_flag, DEV_TIMEOUT_EPILOGUE);
       if (!__all_sync(0xffffffffu, ok)) break;  // warp-uniform exit before the .sync.aligned loads
       tc_fence_after();
-      const int row = m0 + q * 32 + lane;
+      const int rt = q * 32 + lane;  // row inside the tile
+      const int row = m0 + rt;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 16) {
         float v[16];
         tmem_ld16(t_row + c0, v);
         tmem_ld_wait();
-        if (row < sh.M && n0 + c0 < sh.N) epi(row, n0 + c0, v);
+        if constexpr (RES) {
+          // residual from the swizzled box: row rt, 16-byte chunks (c0%32)/4 .. +3
+          float xin[16];
+          const uint8_t* xrow = sX + (c0 / 32) * XBOX_BYTES + rt * 128;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int ch = ((c0 & 31) >> 2) + j;
+            const float4 f = *reinterpret_cast<const float4*>(xrow + ((ch ^ (rt & 7)) << 4));
+            xin[4 * j + 0] = f.x;
+            xin[4 * j + 1] = f.y;
+            xin[4 * j + 2] = f.z;
+            xin[4 * j + 3] = f.w;
+          }
+          if (row < sh.M && n0 + c0 < sh.N) epi(row, n0 + c0, v, xin);
+        } else {
+          if (row < sh.M && n0 + c0 < sh.N) epi(row, n0 + c0, v);
+        }
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
+      if (lane == 0) {
+        mbar_arrive(&tempty[acc]);
+        if (RES) mbar_arrive(x_empty);
+      }
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
+      xph ^= 1u;
     }
   }
 

@@ -33,11 +33,17 @@ int num_sms();
 // box_cols (box_cols * 2 == 128 selects the 128B swizzle).
 bool tmap_bf16(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows,
                uint32_t box_cols);
+// same over fp32 elements (box_cols * 4 == 128 selects the 128B swizzle)
+bool tmap_f32(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows,
+              uint32_t box_cols);
+
+// Query rows per attention CTA (two 128-row sub-tiles).
+constexpr int ATT_Q_ROWS = 256;
 
 struct AttnTile {
   int seq_start;  // first packed row of the sequence
   int seq_len;    // valid frames of the sequence
-  int q0;         // first query of this tile, relative to seq_start
+  int q0;         // first query of this block (multiple of ATT_Q_ROWS), relative to seq_start
   int pad;
 };
 
@@ -50,6 +56,10 @@ int pick_bn(int M, int N);
 // transposed to vt[1024][ldvt] in fp16 (the PV operand of the attention).
 void gemm_qkv(int bn, const CUtensorMap& A, const CUtensorMap& B, int M, int b_off, const float* bias, bf16* q,
               bf16* k, __half* vt, int ldvt, const int* pos, const float2* rope, int* err, cudaStream_t s);
+// x[M,1024] += gate[col] * (A*B^T + bias), residual tile prefetched by TMA
+// through X (fp32 map of x, box 128 rows x 32 cols); B box 128 x 64.
+void gemm_gate_res_tma(const CUtensorMap& A, const CUtensorMap& B, const CUtensorMap& X, int M, int K, int b_off,
+                       const float* bias, const float* gate, float* x, int* err, cudaStream_t s);
 // x[M,1024] += gate[col] * (A*B^T + bias)
 void gemm_gate_res(int bn, const CUtensorMap& A, const CUtensorMap& B, int M, int K, int b_off, const float* bias,
                    const float* gate, float* x, int* err, cudaStream_t s);

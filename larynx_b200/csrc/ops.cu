@@ -61,7 +61,7 @@ int lx_flow_op_attention(int n_seq, const int32_t* lengths, const void* q, const
   int R = 0;
   for (int i = 0; i < n_seq; ++i) {
     if (lengths[i] <= 0) return LX_ERR_ARG;
-    for (int q0 = 0; q0 < lengths[i]; q0 += 128) tiles.push_back(AttnTile{R, lengths[i], q0, 0});
+    for (int q0 = 0; q0 < lengths[i]; q0 += ATT_Q_ROWS) tiles.push_back(AttnTile{R, lengths[i], q0, 0});
     R += (lengths[i] + 7) / 8 * 8;
   }
   const int Rv = (R + 7) / 8 * 8;
