@@ -1,27 +1,27 @@
 // Fused flash attention for the DiT blocks on sm_100a (tcgen05 + TMEM).
 //
 // One CTA = one (sequence, 256-query block, head), head_dim = 64, processed as
-// two 128-row sub-tiles that ping-pong on the tensor core.  Warpgroup 0 is the
-// producer (registers lowered with setmaxnreg), warpgroups 1 and 2 run the
-// softmax of sub-tiles 0 and 1 (registers raised):
+// two independent 128-row sub-tiles.  Warpgroup 0 is the producer (registers
+// lowered with setmaxnreg), warpgroups 1 and 2 run the softmax of sub-tiles 0
+// and 1 (registers raised).  Tensor memory per sub-tile i (256 columns):
+// S_i [0,128), P_i [128,192) (fp16 pairs), O_i [192,256).
 //   warp 0      TMA: both Q sub-tiles once, then per stage the K tile
-//               [128 keys x 64] and the transposed fp16 V tile [64 x 128 keys]
-//   warp 1      TMEM allocation; lane 0 issues, per key tile j and sub-tile i,
-//               S_i = Q_i K_j^T (M=128, N=128, K=64, bf16) into TMEM and
-//               O_i += P_i V_j (M=128, N=64, K=128, fp16) into TMEM, in the
-//               order PV_0,j -> S_0,j+1 -> PV_1,j -> S_1,j+1 so that the
-//               softmax of one sub-tile overlaps the MMAs of the other
-//   warps 2..3  idle
+//               [128 keys x 64] and the fp16 V^T tile [64 x 128 keys]
+//   warp 1+i    (i = 0, 1) issues the MMAs of sub-tile i: S_i = Q_i K_j+1^T
+//               (M=128, N=128, K=64, bf16) as soon as the softmax has pulled
+//               S_i,j into registers, so QK^T of tile j+1 runs under the
+//               softmax of tile j; then O_i += P_i V_j (M=128, N=64, K=128,
+//               fp16, P read from tensor memory).  One issuing thread per
+//               sub-tile: a tcgen05.mma takes ~70 cycles to issue.
+//   warp 3      idle
 //   warps 4..7  softmax of sub-tile 0, warps 8..11 softmax of sub-tile 1:
-//               thread = query row; its S row is pulled from TMEM into
-//               registers (releasing the S columns to the next QK^T at once),
-//               key-padding /
-//               block-causal mask on boundary tiles only, fp32 online softmax
-//               in the exp2 domain, P written as fp16 into shared memory in
-//               the 128B-swizzled K-major layout (P in [0, 256] and V^T are
-//               the fp16 operands of the PV MMA).  O stays in TMEM; it is
-//               rescaled only when a row's running max grows by more than
-//               2^8 (the reference max is otherwise kept, which is exact).
+//               thread = query row; S row from TMEM into registers,
+//               key-padding / block-causal mask on boundary tiles only,
+//               online softmax in the exp2 domain (fp32 row sum), P written
+//               as packed fp16 into its own TMEM columns (P never touches
+//               shared memory, whose bandwidth the MMA operands need).  O is
+//               rescaled in place only when a row's running max grows by more
+//               than 2^8 (the reference max is otherwise kept, which is exact).
 // No score matrix ever reaches HBM.
 #include "common.cuh"
 #include "kernels.h"
@@ -30,38 +30,39 @@ namespace lx {
 
 namespace {
 
-constexpr int ATT_THREADS = 384;  // 3 warpgroups: producer (TMA, MMA, 2 idle), softmax 0, softmax 1
+constexpr int ATT_THREADS = 384;  // 3 warpgroups: producer (TMA, 2 MMA, 1 idle), softmax 0, softmax 1
 // Register split with setmaxnreg: the block is launched with 384 x 168 = 64512
 // registers; producer warpgroup 128 x 56 + softmax warpgroups 256 x 224 = 64512.
 constexpr int REGS_PRODUCER = 56;
 constexpr int REGS_SOFTMAX = 224;
-constexpr int ATT_STAGES = 3;
-constexpr int Q_BYTES = 128 * 64 * 2;   // 16 KB per sub-tile
-constexpr int K_BYTES = 128 * 64 * 2;   // 16 KB
-constexpr int V_BYTES = 64 * 128 * 2;   // 16 KB (two 64-key boxes)
-constexpr int P_BYTES = 128 * 128 * 2;  // 32 KB per sub-tile (two 64-key atoms)
-constexpr int ATT_SMEM = 1024 + 2 * Q_BYTES + ATT_STAGES * (K_BYTES + V_BYTES) + 2 * P_BYTES + 512;
+constexpr int ATT_STAGES = 4;
+constexpr int Q_BYTES = 128 * 64 * 2;  // 16 KB per sub-tile
+constexpr int K_BYTES = 128 * 64 * 2;  // 16 KB
+constexpr int V_BYTES = 64 * 128 * 2;  // 16 KB: two 64-key boxes of V^T (value rows only)
+constexpr int ATT_SMEM = 1024 + 2 * Q_BYTES + ATT_STAGES * (K_BYTES + V_BYTES) + 512;
 constexpr uint32_t ATT_TMEM_COLS = 512;
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units: P <= 2^8
 
-__device__ __forceinline__ uint32_t s_col(int i) { return static_cast<uint32_t>(i * 128); }
-__device__ __forceinline__ uint32_t o_col(int i) { return static_cast<uint32_t>(256 + i * 64); }
+__device__ __forceinline__ uint32_t s_col(int i) { return static_cast<uint32_t>(i * 256); }
+__device__ __forceinline__ uint32_t p_col(int i) { return static_cast<uint32_t>(i * 256 + 128); }
+__device__ __forceinline__ uint32_t o_col(int i) { return static_cast<uint32_t>(i * 256 + 192); }
 
-__device__ __forceinline__ void issue_s(uint32_t d, uint32_t q_addr, uint32_t k_addr) {
+// S = Q K^T from precomputed descriptors (start address advanced by 32 B = 2
+// units per K=16 step; smem addresses stay below 2^18, so no carry leaves the
+// 14-bit start-address field)
+__device__ __forceinline__ void issue_s(uint32_t d, uint64_t dq, uint64_t dk) {
   constexpr uint32_t IDESC_S = idesc_bf16_f32(128, 128);
-#pragma unroll 1
-  for (int k = 0; k < 4; ++k)
-    umma_ss(d, sdesc_sw128(q_addr + k * 32), sdesc_sw128(k_addr + k * 32), IDESC_S, k > 0 ? 1u : 0u);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) umma_ss(d, dq + 2 * k, dk + 2 * k, IDESC_S, k > 0 ? 1u : 0u);
 }
 
-__device__ __forceinline__ void issue_pv(uint32_t d, uint32_t p_addr, uint32_t v_addr, bool accumulate) {
-  constexpr uint32_t IDESC_O = idesc_f16_f32(128, 64);  // P, V^T in fp16
-#pragma unroll 1
-  for (int kk = 0; kk < 8; ++kk) {
-    const uint32_t pa = p_addr + (kk >> 2) * (P_BYTES / 2) + (kk & 3) * 32;
-    const uint32_t va = v_addr + (kk >> 2) * (V_BYTES / 2) + (kk & 3) * 32;
-    umma_ss(d, sdesc_sw128(pa), sdesc_sw128(va), IDESC_O, (accumulate || kk > 0) ? 1u : 0u);
-  }
+// O (+)= P V: P (fp16, 128 keys = 64 TMEM columns) from TMEM, V^T from smem
+__device__ __forceinline__ void issue_pv(uint32_t d, uint32_t p_tmem, uint64_t dv, bool accumulate) {
+  constexpr uint32_t IDESC_O = idesc_f16_f32(128, HDIM);
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk)
+    umma_ts(d, p_tmem + kk * 8, dv + (kk >> 2) * ((V_BYTES / 2) >> 4) + (kk & 3) * 2, IDESC_O,
+            (accumulate || kk > 0) ? 1u : 0u);
 }
 
 __device__ __forceinline__ float ex2(float x) {
@@ -76,18 +77,6 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
   return d;
 }
 
-// (a, b) = (a, b) * s + (c, c) with one packed f32x2 FMA
-__device__ __forceinline__ void fma2(float& a, float& b, float s, float c) {
-  asm("{\n\t.reg .b64 x, y, z, d;\n\t"
-      "mov.b64 x, {%0, %1};\n\t"
-      "mov.b64 y, {%2, %2};\n\t"
-      "mov.b64 z, {%3, %3};\n\t"
-      "fma.rn.f32x2 d, x, y, z;\n\t"
-      "mov.b64 {%0, %1}, d;\n\t}"
-      : "+f"(a), "+f"(b)
-      : "f"(s), "f"(c));
-}
-
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
@@ -99,6 +88,19 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
       "f"(v[27]), "f"(v[28]), "f"(v[29]), "f"(v[30]), "f"(v[31])
       : "memory");
 }
+
+__device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+      "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]),
+      "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]),
+      "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
+}
+
 template <int N>
 __device__ __forceinline__ void regs_dec() {
   asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
@@ -116,11 +118,10 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
                 bf16* __restrict__ out, int* err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;                                  // 2 sub-tiles
+  uint8_t* sQ = smem;  // 2 sub-tiles
   uint8_t* sK = sQ + 2 * Q_BYTES;
   uint8_t* sV = sK + ATT_STAGES * K_BYTES;
-  uint8_t* sP = sV + ATT_STAGES * V_BYTES;             // 2 sub-tiles
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * P_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + ATT_STAGES * V_BYTES);
   uint64_t* q_full = bars;
   uint64_t* kv_full = bars + 1;
   uint64_t* kv_empty = kv_full + ATT_STAGES;
@@ -128,7 +129,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   uint64_t* s_empty = s_full + 2;            // [2]
   uint64_t* p_full = s_empty + 2;            // [2]
   uint64_t* o_done = p_full + 2;             // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 2);
+  uint64_t* turn = o_done + 2;               // [2] exp-phase token between the softmax warpgroups
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(turn + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -148,13 +150,14 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     mbar_init(q_full, 1);
     for (int s = 0; s < ATT_STAGES; ++s) {
       mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+      mbar_init(&kv_empty[s], n_sub);  // one commit per sub-tile's MMA thread
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&s_empty[i], 4);
       mbar_init(&p_full[i], 4);
       mbar_init(&o_done[i], 1);
+      mbar_init(&turn[i], 4);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -185,24 +188,30 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
           mbar_arrive_expect_tx(&kv_full[stage], K_BYTES + V_BYTES);
           const int key0 = tile.seq_start + j * 128;
           tma_load_2d(sK + stage * K_BYTES, &tmK, &kv_full[stage], head * HDIM, key0);
-          tma_load_2d(sV + stage * V_BYTES, &tmV, &kv_full[stage], key0, head * HDIM);
-          tma_load_2d(sV + stage * V_BYTES + V_BYTES / 2, &tmV, &kv_full[stage], key0 + 64, head * HDIM);
+          tma_load_2d(sV + stage * V_BYTES, &tmV, &kv_full[stage], key0, head * VT_ROWS);
+          tma_load_2d(sV + stage * V_BYTES + V_BYTES / 2, &tmV, &kv_full[stage], key0 + 64, head * VT_ROWS);
           if (++stage == ATT_STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
-    }
-    } else if (warp == 1) {
+      }
+    } else if (warp <= 2 && warp - 1 < n_sub) {
       if (lane == 0) {
+        // MMA issue for sub-tile i: S_{j+1} as soon as S_j is in registers, then PV_j
+        const int i = warp - 1;
+        const uint64_t dq = sdesc_sw128(smem_u32(sQ + i * Q_BYTES));
+        const uint64_t dk0 = sdesc_sw128(smem_u32(sK));
+        const uint64_t dv0 = sdesc_sw128(smem_u32(sV));
+        const uint32_t s_t = tmem_base + s_col(i);
+        const uint32_t p_t = tmem_base + p_col(i);
+        const uint32_t o_t = tmem_base + o_col(i);
         bool ok = mbar_wait(q_full, 0, err, abort_flag, DEV_TIMEOUT_MMA);
         if (ok) ok = mbar_wait(&kv_full[0], 0, err, abort_flag, DEV_TIMEOUT_MMA);
         if (ok) {
           tc_fence_after();
-          for (int i = 0; i < n_sub; ++i) {
-            issue_s(tmem_base + s_col(i), smem_u32(sQ + i * Q_BYTES), smem_u32(sK));
-            umma_commit(&s_full[i]);
-          }
+          issue_s(s_t, dq, dk0);
+          umma_commit(&s_full[i]);
         }
         int stage = 0;
         uint32_t phase = 0;
@@ -213,24 +222,20 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
             st_n = 0;
             ph_n ^= 1u;
           }
-          for (int i = 0; ok && i < n_sub; ++i) {
-            // O_i += P_i V_j once the softmax has published P_i (and rescaled O_i)
-            ok = mbar_wait(&p_full[i], static_cast<uint32_t>(j & 1), err, abort_flag, DEV_TIMEOUT_MMA);
+          if (j + 1 < nkv) {
+            ok = mbar_wait(&kv_full[st_n], ph_n, err, abort_flag, DEV_TIMEOUT_MMA);
+            if (ok) ok = mbar_wait(&s_empty[i], static_cast<uint32_t>(j & 1), err, abort_flag, DEV_TIMEOUT_MMA);
             if (!ok) break;
             tc_fence_after();
-            issue_pv(tmem_base + o_col(i), smem_u32(sP + i * P_BYTES), smem_u32(sV + stage * V_BYTES), j > 0);
-            umma_commit(&o_done[i]);
-            if (i == n_sub - 1) umma_commit(&kv_empty[stage]);
-            // S_i for the next key tile, once the softmax has pulled S_i into registers
-            if (j + 1 < nkv) {
-              if (i == 0) ok = mbar_wait(&kv_full[st_n], ph_n, err, abort_flag, DEV_TIMEOUT_MMA);
-              if (ok) ok = mbar_wait(&s_empty[i], static_cast<uint32_t>(j & 1), err, abort_flag, DEV_TIMEOUT_MMA);
-              if (!ok) break;
-              tc_fence_after();
-              issue_s(tmem_base + s_col(i), smem_u32(sQ + i * Q_BYTES), smem_u32(sK + st_n * K_BYTES));
-              umma_commit(&s_full[i]);
-            }
+            issue_s(s_t, dq, dk0 + static_cast<uint64_t>((st_n * K_BYTES) >> 4));
+            umma_commit(&s_full[i]);
           }
+          ok = mbar_wait(&p_full[i], static_cast<uint32_t>(j & 1), err, abort_flag, DEV_TIMEOUT_MMA);
+          if (!ok) break;
+          tc_fence_after();
+          issue_pv(o_t, p_t, dv0 + static_cast<uint64_t>((stage * V_BYTES) >> 4), j > 0);
+          umma_commit(&o_done[i]);
+          umma_commit(&kv_empty[stage]);
           stage = st_n;
           phase = ph_n;
         }
@@ -246,9 +251,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     const int q_chunk = chunk > 0 ? qi / chunk : 0;
     const float sl2 = 0.125f * 1.4426950408889634f;  // 1/sqrt(64) * log2(e)
     const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
-    uint8_t* p_tile = sP + sub * P_BYTES;
     float m_ref = -INFINITY;  // reference max, scaled (log2) units
-    float l = 0.f;
+    float l = 0.f;            // row sum of P relative to m_ref
     bool ok = sub < n_sub;
     for (int j = 0; ok && j < nkv; ++j) {
       ok = mbar_wait(&s_full[sub], static_cast<uint32_t>(j & 1), err, abort_flag, DEV_TIMEOUT_SOFTMAX);
@@ -290,18 +294,17 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       const float rmax = max3(max3(mx[0], mx[1], mx[2]), max3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
       const float m_cand = rmax * sl2;
       const bool need = m_cand > m_ref + RESCALE_THRESHOLD;  // false when rmax == -inf
-      // O_{sub} for key tile j-1 must be complete before it is rescaled and
-      // before P_j overwrites the P tile that PV_{j-1} reads
-      if (j > 0) {
-        ok = mbar_wait(&o_done[sub], static_cast<uint32_t>((j - 1) & 1), err, abort_flag, DEV_TIMEOUT_SOFTMAX);
-        ok = __all_sync(0xffffffffu, ok);
-        if (!ok) break;
-        tc_fence_after();
-      }
+      bool waited = false;
       if (__any_sync(0xffffffffu, need)) {
         const float new_ref = need ? m_cand : m_ref;
         const float alpha = need ? ex2(m_ref - new_ref) : 1.0f;  // 0 from -inf
         if (j > 0) {
+          // PV_{j-1} is the last update of O before this in-place rescale
+          ok = mbar_wait(&o_done[sub], static_cast<uint32_t>((j - 1) & 1), err, abort_flag, DEV_TIMEOUT_SOFTMAX);
+          ok = __all_sync(0xffffffffu, ok);
+          if (!ok) break;
+          tc_fence_after();
+          waited = true;
 #pragma unroll 1
           for (int h = 0; h < 2; ++h) {
             float t[32];
@@ -317,27 +320,49 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         m_ref = new_ref;
       }
       const float m_use = (m_ref == -INFINITY) ? 0.f : m_ref;
-      // p = 2^(s*scale - m), row sum, fp16 P into the swizzled tile
+      // The two softmax warpgroups take turns for the exponentials (they share
+      // the MUFU units of each SM sub-partition): sub-tile 0 goes first, then
+      // each passes the turn on, so one's exp phase overlaps the other's loads,
+      // max and stores.
+      if (n_sub == 2 && (sub == 1 || j > 0)) {
+        ok = mbar_wait(&turn[sub], static_cast<uint32_t>((sub == 0 ? j - 1 : j) & 1), err, abort_flag,
+                       DEV_TIMEOUT_SOFTMAX);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+      }
+      // p = 2^(s*scale - m) in fp32, row sum in fp32, P packed as fp16 pairs
       float rs[4] = {0.f, 0.f, 0.f, 0.f};
-      uint8_t* prow = p_tile + r * 128;
+      uint32_t pk[64];
 #pragma unroll
-      for (int ch = 0; ch < 16; ++ch) {
-#pragma unroll
-        for (int i = 0; i < 8; i += 2) {
-          fma2(s[ch * 8 + i], s[ch * 8 + i + 1], sl2, -m_use);
-          s[ch * 8 + i] = ex2(s[ch * 8 + i]);
-          s[ch * 8 + i + 1] = ex2(s[ch * 8 + i + 1]);
-          rs[(i >> 1) & 3] += s[ch * 8 + i] + s[ch * 8 + i + 1];
-        }
-        uint4 pk;
-        pk.x = pack_f16x2(s[ch * 8 + 0], s[ch * 8 + 1]);
-        pk.y = pack_f16x2(s[ch * 8 + 2], s[ch * 8 + 3]);
-        pk.z = pack_f16x2(s[ch * 8 + 4], s[ch * 8 + 5]);
-        pk.w = pack_f16x2(s[ch * 8 + 6], s[ch * 8 + 7]);
-        *reinterpret_cast<uint4*>(prow + (ch >> 3) * (P_BYTES / 2) + (((ch & 7) ^ (r & 7)) << 4)) = pk;
+      for (int i = 0; i < 64; ++i) {
+        const float p0 = ex2(fmaf(s[2 * i], sl2, -m_use));
+        const float p1 = ex2(fmaf(s[2 * i + 1], sl2, -m_use));
+        rs[i & 3] += p0 + p1;
+        pk[i] = pack_f16x2(p0, p1);
       }
       l += (rs[0] + rs[1]) + (rs[2] + rs[3]);
-      fence_proxy_async_smem();
+      if (n_sub == 2) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&turn[sub ^ 1]);
+      }
+      // PV_{j-1} must have read P_{j-1} before P_j replaces it
+      if (j > 0 && !waited) {
+        ok = mbar_wait(&o_done[sub], static_cast<uint32_t>((j - 1) & 1), err, abort_flag, DEV_TIMEOUT_SOFTMAX);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        tc_fence_after();
+      }
+      {
+        uint32_t h0[32], h1[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          h0[i] = pk[i];
+          h1[i] = pk[32 + i];
+        }
+        tmem_st32u(t_lane + p_col(sub), h0);
+        tmem_st32u(t_lane + p_col(sub) + 32, h1);
+      }
+      tmem_st_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[sub]);
@@ -347,27 +372,27 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       ok = __all_sync(0xffffffffu, ok);
       if (ok) {
         tc_fence_after();
-        const float inv = 1.0f / l;
         float o[64];
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           float t[32];
           tmem_ld32(t_lane + o_col(sub) + h * 32, t);
-          tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[h * 32 + i] = t[i] * inv;
+          for (int i = 0; i < 32; ++i) o[h * 32 + i] = t[i];
         }
+        tmem_ld_wait();
+        const float inv = 1.0f / l;
         if (r < (sub == 0 ? nq0 : nq1)) {
           uint4* dst =
               reinterpret_cast<uint4*>(out + static_cast<size_t>(tile.seq_start + qi) * DIM + head * HDIM);
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
-            uint4 pk;
-            pk.x = pack_bf16x2(o[c * 8 + 0], o[c * 8 + 1]);
-            pk.y = pack_bf16x2(o[c * 8 + 2], o[c * 8 + 3]);
-            pk.z = pack_bf16x2(o[c * 8 + 4], o[c * 8 + 5]);
-            pk.w = pack_bf16x2(o[c * 8 + 6], o[c * 8 + 7]);
-            dst[c] = pk;
+            uint4 pk4;
+            pk4.x = pack_bf16x2(o[c * 8 + 0] * inv, o[c * 8 + 1] * inv);
+            pk4.y = pack_bf16x2(o[c * 8 + 2] * inv, o[c * 8 + 3] * inv);
+            pk4.z = pack_bf16x2(o[c * 8 + 4] * inv, o[c * 8 + 5] * inv);
+            pk4.w = pack_bf16x2(o[c * 8 + 6] * inv, o[c * 8 + 7] * inv);
+            dst[c] = pk4;
           }
         }
       }

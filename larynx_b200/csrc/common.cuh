@@ -138,6 +138,18 @@ __device__ __forceinline__ void umma_ss(uint32_t d_tmem, uint64_t adesc, uint64_
       : "memory");
 }
 
+// D(tmem) (+)= A(tmem) * B(smem)^T: A is K-major in tensor memory (row m in
+// lane m, two 16-bit K elements per 32-bit column).
+__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive (once) on the mbarrier when all previously issued tcgen05 ops of
 // this thread have completed.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
@@ -221,6 +233,17 @@ __device__ __forceinline__ float gelu_tanh_f(float x) {
   const float c1 = 0.7978845608028654f;
   const float c0 = 0.044715f;
   return 0.5f * x * (1.0f + tanhf(c1 * (x + c0 * x * x * x)));
+}
+
+// Same GELU with the hardware tanh approximation (one MUFU op; its error,
+// ~2^-11 relative, is below the bf16 rounding of the GEMM epilogue output).
+__device__ __forceinline__ float gelu_tanh_fast(float x) {
+  const float c1 = 0.7978845608028654f;
+  const float c0 = 0.044715f;
+  float t;
+  const float u = c1 * (x + c0 * x * x * x);
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(u));
+  return 0.5f * x * (1.0f + t);
 }
 
 // Mish = x * tanh(softplus(x)); softplus with torch's threshold 20.

@@ -479,7 +479,7 @@ int ensure_workspace(lx_flow* h, const Plan& p, size_t in_floats, int n_utt) {
     int rc;
     if ((rc = dev_alloc(h, &w.x, R * DIM, false)) || (rc = dev_alloc(h, &w.xn, R * DIM, false)) ||
         (rc = dev_alloc(h, &w.q, R * DIM, false)) || (rc = dev_alloc(h, &w.k, R * DIM, false)) ||
-        (rc = dev_alloc(h, &w.vt, static_cast<size_t>(DIM) * w.Rv, false)) ||
+        (rc = dev_alloc(h, &w.vt, static_cast<size_t>(HEADS) * VT_ROWS * w.Rv, false)) ||
         (rc = dev_alloc(h, &w.ao, R * DIM, false)) || (rc = dev_alloc(h, &w.h, R * FF, false)) ||
         (rc = dev_alloc(h, &w.stage1, Rs * DIM, false)) || (rc = dev_alloc(h, &w.stage2, Rs * DIM, false)) ||
         (rc = dev_alloc(h, &w.cst, R * DIM, false)) || (rc = dev_alloc(h, &w.a_cond, R * COND_K, false)) ||
@@ -499,7 +499,7 @@ int ensure_workspace(lx_flow* h, const Plan& p, size_t in_floats, int n_utt) {
     CK(cudaMemset(w.xn, 0, R * DIM * 2));
     CK(cudaMemset(w.q, 0, R * DIM * 2));
     CK(cudaMemset(w.k, 0, R * DIM * 2));
-    CK(cudaMemset(w.vt, 0, static_cast<size_t>(DIM) * w.Rv * 2));
+    CK(cudaMemset(w.vt, 0, static_cast<size_t>(HEADS) * VT_ROWS * w.Rv * 2));
     CK(cudaMemset(w.ao, 0, R * DIM * 2));
     CK(cudaMemset(w.h, 0, R * FF * 2));
     CK(cudaMemset(w.stage1, 0, Rs * DIM * 2));
@@ -515,7 +515,7 @@ int ensure_workspace(lx_flow* h, const Plan& p, size_t in_floats, int n_utt) {
     ok &= tmap_bf16(&w.tm_stage2, w.stage2, Rs, DIM, DIM, 128, 64);
     ok &= tmap_bf16(&w.tm_q, w.q, R, DIM, DIM, 128, 64);
     ok &= tmap_bf16(&w.tm_k, w.k, R, DIM, DIM, 128, 64);
-    ok &= tmap_bf16(&w.tm_vt, w.vt, DIM, w.Rv, w.Rv, 64, 64);
+    ok &= tmap_bf16(&w.tm_vt, w.vt, static_cast<uint64_t>(HEADS) * VT_ROWS, w.Rv, w.Rv, VT_ROWS, 64);
     ok &= tmap_f32(&w.tm_x, w.x, R, DIM, DIM, 128, 32);
     if (!ok) return h->fail(LX_ERR_CUDA, "cuTensorMapEncodeTiled failed for a workspace tensor");
     ++w.generation;

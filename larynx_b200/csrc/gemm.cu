@@ -128,7 +128,7 @@ struct EpiQKV {
       }
       store_bf16x16((which == 0 ? q : k) + static_cast<size_t>(row) * DIM + c, v);
     } else {
-      __half* dst = vt + static_cast<size_t>(c) * ldvt + row;
+      __half* dst = vt + static_cast<size_t>((c >> 6) * VT_ROWS + (c & 63)) * ldvt + row;
 #pragma unroll
       for (int j = 0; j < 16; ++j) dst[static_cast<size_t>(j) * ldvt] = __float2half_rn(v[j]);
     }
@@ -187,7 +187,7 @@ struct EpiGelu {
   __device__ __forceinline__ void operator()(int row, int col0, float (&v)[16]) const {
     add_bias16(v, bias + col0);
 #pragma unroll
-    for (int j = 0; j < 16; ++j) v[j] = gelu_tanh_f(v[j]);
+    for (int j = 0; j < 16; ++j) v[j] = gelu_tanh_fast(v[j]);
     store_bf16x16(h + static_cast<size_t>(row) * FF + col0, v);
   }
 };

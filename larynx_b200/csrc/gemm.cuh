@@ -53,6 +53,31 @@ __host__ __device__ constexpr int gemm_smem_bytes() {
          (MODE == MODE_RESID ? GEMM_BM * BN * 4 : 0) + 256 /*barriers*/;
 }
 
+// One 16-column chunk of the epilogue (residual from the swizzled smem tile
+// when RES).
+template <bool RES, class Epi>
+__device__ __forceinline__ void epi_chunk(const Epi& epi, const uint8_t* sX, int rt, int row, int n0, int c0,
+                                          const GemmShape& sh, float (&v)[16]) {
+  constexpr int XBOX_BYTES = 128 * 32 * 4;
+  if (row >= sh.M || n0 + c0 >= sh.N) return;
+  if constexpr (RES) {
+    float xin[16];
+    const uint8_t* xrow = sX + (c0 / 32) * XBOX_BYTES + rt * 128;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int ch = ((c0 & 31) >> 2) + j;
+      const float4 f = *reinterpret_cast<const float4*>(xrow + ((ch ^ (rt & 7)) << 4));
+      xin[4 * j + 0] = f.x;
+      xin[4 * j + 1] = f.y;
+      xin[4 * j + 2] = f.z;
+      xin[4 * j + 3] = f.w;
+    }
+    epi(row, n0 + c0, v, xin);
+  } else {
+    epi(row, n0 + c0, v);
+  }
+}
+
 template <int BN, int STAGES, int MODE, class Epi>
 __global__ void __launch_bounds__(gemm_threads(MODE), 1)
     k_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -149,6 +174,9 @@ __global__ void __launch_bounds__(gemm_threads(MODE), 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
+      // descriptors of stage 0; stage s and K step k add (s * bytes + 32 k) >> 4
+      const uint64_t da0 = sdesc_sw128(smem_u32(sA));
+      const uint64_t db0 = sdesc_sw128(smem_u32(sB));
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -164,13 +192,11 @@ __global__ void __launch_bounds__(gemm_threads(MODE), 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(sA + stage * A_BYTES);
-          const uint32_t b_addr = smem_u32(sB + stage * B_BYTES);
+          const uint64_t da = da0 + static_cast<uint64_t>((stage * A_BYTES) >> 4);
+          const uint64_t db = db0 + static_cast<uint64_t>((stage * B_BYTES) >> 4);
 #pragma unroll
-          for (int k = 0; k < GEMM_BK / 16; ++k) {
-            umma_ss(d_tmem, sdesc_sw128(a_addr + k * 32), sdesc_sw128(b_addr + k * 32), IDESC,
-                    (kb > 0 || k > 0) ? 1u : 0u);
-          }
+          for (int k = 0; k < GEMM_BK / 16; ++k)
+            umma_ss(d_tmem, da + 2 * k, db + 2 * k, IDESC, (kb > 0 || k > 0) ? 1u : 0u);
           umma_commit(&empty[stage]);
           if (++stage == STAGES) {
             stage = 0;
@@ -213,28 +239,20 @@ __global__ void __launch_bounds__(gemm_threads(MODE), 1)
       const int rt = q * 32 + lane;  // row inside the tile
       const int row = m0 + rt;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      // software-pipelined: the TMEM load of chunk c+1 is in flight while
+      // chunk c is processed (tcgen05.wait::ld waits for all of this thread's loads)
+      float va[16], vb[16];
+      tmem_ld16(t_row, va);
+      tmem_ld_wait();
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 16) {
-        float v[16];
-        tmem_ld16(t_row + c0, v);
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        if (c0 + 16 < BN) tmem_ld16(t_row + c0 + 16, vb);
+        epi_chunk<RES>(epi, sX, rt, row, n0, c0, sh, va);
         tmem_ld_wait();
-        if constexpr (RES) {
-          // residual from the swizzled box: row rt, 16-byte chunks (c0%32)/4 .. +3
-          float xin[16];
-          const uint8_t* xrow = sX + (c0 / 32) * XBOX_BYTES + rt * 128;
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int ch = ((c0 & 31) >> 2) + j;
-            const float4 f = *reinterpret_cast<const float4*>(xrow + ((ch ^ (rt & 7)) << 4));
-            xin[4 * j + 0] = f.x;
-            xin[4 * j + 1] = f.y;
-            xin[4 * j + 2] = f.z;
-            xin[4 * j + 3] = f.w;
-          }
-          if (row < sh.M && n0 + c0 < sh.N) epi(row, n0 + c0, v, xin);
-        } else {
-          if (row < sh.M && n0 + c0 < sh.N) epi(row, n0 + c0, v);
-        }
+        if (c0 + 16 >= BN) break;
+        if (c0 + 32 < BN) tmem_ld16(t_row + c0 + 32, va);
+        epi_chunk<RES>(epi, sX, rt, row, n0, c0 + 16, sh, vb);
+        tmem_ld_wait();
       }
       tc_fence_before();
       __syncwarp();

@@ -24,6 +24,8 @@ constexpr int MOD_N = 6 * DIM;
 constexpr int CONV_K = 31;
 constexpr int CONV_G = 16;
 constexpr int COND_K = 3 * MEL;  // [cond, mu, spks] columns of the input projection
+// V^T rows per head (value channels)
+constexpr int VT_ROWS = 64;
 
 // Number of SMs of the current device (cached per device).
 int num_sms();

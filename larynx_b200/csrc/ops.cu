@@ -16,7 +16,8 @@ __global__ void k_transpose_v(const bf16* __restrict__ v, __half* __restrict__ v
   const int r = blockIdx.x * 32 + threadIdx.x;
   const int c = blockIdx.y * 32 + threadIdx.y;
   if (r < R && c < DIM)
-    vt[static_cast<size_t>(c) * ldvt + r] = __float2half_rn(__bfloat162float(v[static_cast<size_t>(r) * DIM + c]));
+    vt[static_cast<size_t>((c >> 6) * VT_ROWS + (c & 63)) * ldvt + r] =
+        __float2half_rn(__bfloat162float(v[static_cast<size_t>(r) * DIM + c]));
 }
 
 int sync_check(cudaStream_t s, int* d_err) {
@@ -69,18 +70,18 @@ int lx_flow_op_attention(int n_seq, const int32_t* lengths, const void* q, const
   AttnTile* d_tiles = nullptr;
   int* d_err = nullptr;
   int rc = LX_OK;
-  if (cudaMalloc(&vt, static_cast<size_t>(DIM) * Rv * 2) != cudaSuccess ||
+  if (cudaMalloc(&vt, static_cast<size_t>(HEADS) * VT_ROWS * Rv * 2) != cudaSuccess ||
       cudaMalloc(&d_tiles, tiles.size() * sizeof(AttnTile)) != cudaSuccess ||
       cudaMalloc(&d_err, sizeof(int)) != cudaSuccess) {
     rc = LX_ERR_OOM;
   } else {
-    cudaMemsetAsync(vt, 0, static_cast<size_t>(DIM) * Rv * 2, s);
+    cudaMemsetAsync(vt, 0, static_cast<size_t>(HEADS) * VT_ROWS * Rv * 2, s);
     cudaMemsetAsync(d_err, 0, sizeof(int), s);
     cudaMemcpyAsync(d_tiles, tiles.data(), tiles.size() * sizeof(AttnTile), cudaMemcpyHostToDevice, s);
     k_transpose_v<<<dim3((R + 31) / 32, DIM / 32), dim3(32, 32), 0, s>>>(static_cast<const bf16*>(v), vt, R, Rv);
     CUtensorMap tq, tk, tv;
     if (!tmap_bf16(&tq, q, R, DIM, DIM, 128, 64) || !tmap_bf16(&tk, k, R, DIM, DIM, 128, 64) ||
-        !tmap_bf16(&tv, vt, DIM, Rv, Rv, 64, 64)) {
+        !tmap_bf16(&tv, vt, static_cast<uint64_t>(HEADS) * VT_ROWS, Rv, Rv, VT_ROWS, 64)) {
       rc = LX_ERR_ARG;
     } else {
       attention(tq, tk, tv, d_tiles, static_cast<int>(tiles.size()), chunk, static_cast<bf16*>(out), d_err, s);
