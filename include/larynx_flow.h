@@ -173,6 +173,24 @@ int lx_flow_op_gemm(int M, int N, int K, const void* A, const void* B, const flo
 int lx_flow_op_attention(int n_seq, const int32_t* lengths, const void* q, const void* k, const void* v, void* out,
                          int chunk, void* stream);
 
+/* ---- lx_flow_op_attention without device allocation ----------------------
+ * No counterpart in the reference: it exists for callers that may not
+ * allocate device memory on the call path (cudaMalloc / cudaFree can stall on
+ * other streams' work and take unbounded time; a deadline-bound audio loop or
+ * an embedder owning all of HBM through its own pool cannot accept that).
+ * Same arguments, result and synchronous behaviour as lx_flow_op_attention,
+ * but all scratch (V^T copy, tile list, error word) lives in fixed static
+ * device storage (8 MiB + 8 KiB per device), so the call allocates nothing.
+ * Limit: packed rows sum_i round_up(len_i, 8) <= LX_STATIC_ATT_MAX_ROWS,
+ * else LX_ERR_ARG with no device work queued.  The first call on a device (with
+ * that device current) looks the storage up with cudaGetSymbolAddress: make
+ * it before any stream capture.  The storage is shared per device: calls that
+ * overlap in time on one device (two threads, or two streams) race and give
+ * wrong results, so serialise them. */
+#define LX_STATIC_ATT_MAX_ROWS 4096
+int lx_flow_op_attention_static(int n_seq, const int32_t* lengths, const void* q, const void* k, const void* v,
+                                void* out, int chunk, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

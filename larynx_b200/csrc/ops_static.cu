@@ -1,0 +1,124 @@
+// lx_flow_op_attention_static: the flash-attention entry point of ops.cu with
+// every piece of device scratch held in file-scope __device__ arrays, so a call
+// allocates no device memory at all (no cudaMalloc / cudaFree, no allocating
+// library routine).
+//
+// Who needs it: callers that may not allocate device memory on the call path.
+// cudaMalloc / cudaFree can block on, or synchronise with, work the caller has
+// queued on other streams, and take unbounded time; an audio pipeline with a
+// per-chunk deadline, or an embedder that hands the whole of HBM to its own
+// pool allocator up front, cannot accept either.  lx_flow_op_attention
+// allocates its V^T copy, tile list and error word on every call; this entry
+// point uses fixed static storage instead.
+//
+// Limit (checked on the host; a larger call returns LX_ERR_ARG before any
+// device work is queued): packed rows R = sum_i round_up(len_i, 8) <=
+// LX_STATIC_ATT_MAX_ROWS (4096).  Query tiles = sum_i ceil(len_i / 256) <= R / 8,
+// so 512 tile slots always suffice.  The static storage is 8 MiB of V^T
+// (fp16 [1024][4096]) + 8 KiB of tiles + one error word per device.
+//
+// Set-up: the first call on a device (with that device current) resolves the
+// arrays' addresses with cudaGetSymbolAddress, which can load the module; make
+// that first call before any stream capture begins.  Later calls do no set-up.
+//
+// Zero state: only the error word must start at zero; each call clears it on
+// the caller's stream before the kernels run.  Every V^T column the attention
+// reads inside [0, R) is rewritten by the call's transpose, and keys past R
+// come from the tensor map's zero fill, so nothing else needs clearing.
+//
+// Concurrency: the storage is shared by every call on a device.  Calls that
+// overlap in time on one device (from two host threads, or from two streams)
+// race on it and produce wrong results; serialise them.  Each call is
+// synchronous on its stream, so calls made one after another from one thread
+// are safe.
+#include <mutex>
+
+#include "../../include/larynx_flow.h"
+#include "kernels.h"
+
+using namespace lx;
+
+namespace {
+
+constexpr int kMaxRows = LX_STATIC_ATT_MAX_ROWS;
+constexpr int kMaxTiles = kMaxRows / 8;
+constexpr int kMaxDevices = 64;
+
+__device__ __align__(256) __half g_vt[static_cast<size_t>(HEADS) * VT_ROWS * kMaxRows];
+__device__ __align__(256) AttnTile g_tiles[kMaxTiles];
+__device__ __align__(256) int g_err[1];
+
+struct Scratch {
+  __half* vt = nullptr;
+  AttnTile* tiles = nullptr;
+  int* err = nullptr;
+};
+
+std::mutex g_setup_mu;
+Scratch g_scratch[kMaxDevices];
+bool g_ready[kMaxDevices] = {false};
+
+// Resolves the static arrays of the current device once.
+int scratch_for_current_device(Scratch* out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return LX_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(g_setup_mu);
+  if (!g_ready[dev]) {
+    Scratch s;
+    if (cudaGetSymbolAddress(reinterpret_cast<void**>(&s.vt), g_vt) != cudaSuccess ||
+        cudaGetSymbolAddress(reinterpret_cast<void**>(&s.tiles), g_tiles) != cudaSuccess ||
+        cudaGetSymbolAddress(reinterpret_cast<void**>(&s.err), g_err) != cudaSuccess)
+      return LX_ERR_CUDA;
+    g_scratch[dev] = s;
+    g_ready[dev] = true;
+  }
+  *out = g_scratch[dev];
+  return LX_OK;
+}
+
+// v[R][1024] bf16 -> vt[(c/64)*64 + c%64][ldvt] fp16: the same layout the
+// attention kernel's PV operand tensor map describes.
+__global__ void k_transpose_v_static(const bf16* __restrict__ v, __half* __restrict__ vt, int R, int ldvt) {
+  const int r = blockIdx.x * 32 + threadIdx.x;
+  const int c = blockIdx.y * 32 + threadIdx.y;
+  if (r < R && c < DIM)
+    vt[static_cast<size_t>((c >> 6) * VT_ROWS + (c & 63)) * ldvt + r] =
+        __float2half_rn(__bfloat162float(v[static_cast<size_t>(r) * DIM + c]));
+}
+
+}  // namespace
+
+extern "C" int lx_flow_op_attention_static(int n_seq, const int32_t* lengths, const void* q, const void* k,
+                                           const void* v, void* out, int chunk, void* stream) {
+  if (n_seq <= 0 || !lengths || !q || !k || !v || !out || chunk < 0) return LX_ERR_ARG;
+  AttnTile tiles[kMaxTiles];
+  int n_tiles = 0;
+  long long R = 0;
+  for (int i = 0; i < n_seq; ++i) {
+    if (lengths[i] <= 0) return LX_ERR_ARG;
+    for (int q0 = 0; q0 < lengths[i]; q0 += ATT_Q_ROWS) {
+      if (n_tiles >= kMaxTiles) return LX_ERR_ARG;
+      tiles[n_tiles++] = AttnTile{static_cast<int>(R), lengths[i], q0, 0};
+    }
+    R += (lengths[i] + 7) / 8 * 8;
+    if (R > kMaxRows) return LX_ERR_ARG;
+  }
+  Scratch sc;
+  if (int rc = scratch_for_current_device(&sc)) return rc;
+  const int rows = static_cast<int>(R);  // a multiple of 8: the V^T row stride
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  CUtensorMap tq, tk, tv;
+  if (!tmap_bf16(&tq, q, rows, DIM, DIM, 128, 64) || !tmap_bf16(&tk, k, rows, DIM, DIM, 128, 64) ||
+      !tmap_bf16(&tv, sc.vt, static_cast<uint64_t>(HEADS) * VT_ROWS, rows, rows, VT_ROWS, 64))
+    return LX_ERR_ARG;
+  if (cudaMemsetAsync(sc.err, 0, sizeof(int), s) != cudaSuccess ||
+      cudaMemcpyAsync(sc.tiles, tiles, n_tiles * sizeof(AttnTile), cudaMemcpyHostToDevice, s) != cudaSuccess)
+    return LX_ERR_CUDA;
+  k_transpose_v_static<<<dim3((rows + 31) / 32, DIM / 32), dim3(32, 32), 0, s>>>(static_cast<const bf16*>(v), sc.vt,
+                                                                                rows, rows);
+  attention(tq, tk, tv, sc.tiles, n_tiles, chunk, static_cast<bf16*>(out), sc.err, s);
+  if (cudaGetLastError() != cudaSuccess || cudaStreamSynchronize(s) != cudaSuccess) return LX_ERR_CUDA;
+  int e = 0;
+  if (cudaMemcpy(&e, sc.err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return LX_ERR_CUDA;
+  return e ? LX_ERR_TIMEOUT : LX_OK;
+}

@@ -31,7 +31,7 @@ ERRORS = {1: "LX_ERR_ARG", 2: "LX_ERR_IO", 3: "LX_ERR_FORMAT", 4: "LX_ERR_SHAPE"
 EXPORTS = ("lx_flow_create", "lx_flow_destroy", "lx_flow_last_error", "lx_flow_load_gguf", "lx_flow_load_noise",
            "lx_flow_infer", "lx_flow_decode", "lx_flow_decode_device", "lx_flow_estimator",
            "lx_flow_launch_count", "lx_flow_op", "lx_flow_op_gemm", "lx_flow_op_attention",
-           "lx_flow_profile_decode")
+           "lx_flow_profile_decode", "lx_flow_op_attention_static")
 
 KERNEL_CLASSES = ("in_proj", "conv_pos", "adaln", "qkv_gemm", "attention", "out_gemm", "ff1_gemm", "ff2_gemm",
                   "proj_out_gemm", "euler", "other")
@@ -85,7 +85,8 @@ def load_library(path: str = LIB_PATH):
     lib.lx_flow_profile_decode.restype = ctypes.c_int
     lib.lx_flow_op_gemm.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, vp, vp, vp, vp, vp]
     lib.lx_flow_op_attention.argtypes = [ctypes.c_int, _i32p, vp, vp, vp, vp, ctypes.c_int, vp]
-    for name in ("lx_flow_op_gemm", "lx_flow_op_attention", "lx_flow_create", "lx_flow_load_gguf", "lx_flow_load_noise", "lx_flow_infer", "lx_flow_decode",
+    lib.lx_flow_op_attention_static.argtypes = [ctypes.c_int, _i32p, vp, vp, vp, vp, ctypes.c_int, vp]
+    for name in ("lx_flow_op_gemm", "lx_flow_op_attention", "lx_flow_op_attention_static", "lx_flow_create", "lx_flow_load_gguf", "lx_flow_load_noise", "lx_flow_infer", "lx_flow_decode",
                  "lx_flow_decode_device", "lx_flow_estimator", "lx_flow_op"):
         getattr(lib, name).restype = ctypes.c_int
     _lib = lib
@@ -282,3 +283,16 @@ def op_attention(lengths, q_ptr: int, k_ptr: int, v_ptr: int, out_ptr: int, chun
                                   int(chunk), v(stream))
     if rc != LX_OK:
         raise FlowError(f"lx_flow_op_attention failed: {ERRORS.get(rc, rc)}")
+
+
+def op_attention_static(lengths, q_ptr: int, k_ptr: int, v_ptr: int, out_ptr: int, chunk: int = 0,
+                        stream: int = 0) -> None:
+    """``op_attention`` for callers that may not allocate device memory: the
+    scratch is fixed static device storage (packed rows <= 4096).  Calls that overlap in time on one device race on that storage."""
+    lib = load_library()
+    L = np.ascontiguousarray(np.asarray(lengths, dtype=np.int32))
+    v = lambda p: ctypes.c_void_p(p) if p else None
+    rc = lib.lx_flow_op_attention_static(int(L.size), L.ctypes.data_as(_i32p), v(q_ptr), v(k_ptr), v(v_ptr),
+                                         v(out_ptr), int(chunk), v(stream))
+    if rc != LX_OK:
+        raise FlowError(f"lx_flow_op_attention_static failed: {ERRORS.get(rc, rc)}")
