@@ -179,7 +179,7 @@ int lx_flow_op_attention(int n_seq, const int32_t* lengths, const void* q, const
  * other streams' work and take unbounded time; a deadline-bound audio loop or
  * an embedder owning all of HBM through its own pool cannot accept that).
  * Same arguments, result and synchronous behaviour as lx_flow_op_attention,
- * but all scratch (V^T copy, tile list, error word) lives in fixed static
+ * but all scratch (fp16 copy of V, tile list, error word) lives in fixed static
  * device storage (8 MiB + 8 KiB per device), so the call allocates nothing.
  * Limit: packed rows sum_i round_up(len_i, 8) <= LX_STATIC_ATT_MAX_ROWS,
  * else LX_ERR_ARG with no device work queued.  The first call on a device (with

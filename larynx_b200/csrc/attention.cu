@@ -6,7 +6,9 @@
 // and 1 (registers raised).  Tensor memory per sub-tile i (256 columns):
 // S_i [0,128), P_i [128,192) (fp16 pairs), O_i [192,256).
 //   warp 0      TMA: both Q sub-tiles once, then per stage the K tile
-//               [128 keys x 64] and the fp16 V^T tile [64 x 128 keys]
+//               [128 keys x 64] (bf16) and the V tile [128 keys x 64] (fp16,
+//               row-major as the QKV GEMM wrote it; the PV MMA reads it as
+//               an MN-major operand, so no transpose exists anywhere)
 //   warp 1+i    (i = 0, 1) issues the MMAs of sub-tile i: S_i = Q_i K_j+1^T
 //               (M=128, N=128, K=64, bf16) as soon as the softmax has pulled
 //               S_i,j into registers, so QK^T of tile j+1 runs under the
@@ -38,7 +40,7 @@ constexpr int REGS_SOFTMAX = 224;
 constexpr int ATT_STAGES = 4;
 constexpr int Q_BYTES = 128 * 64 * 2;  // 16 KB per sub-tile
 constexpr int K_BYTES = 128 * 64 * 2;  // 16 KB
-constexpr int V_BYTES = 64 * 128 * 2;  // 16 KB: two 64-key boxes of V^T (value rows only)
+constexpr int V_BYTES = 128 * 64 * 2;  // 16 KB: 128 keys x 64 fp16 values (MN-major B of PV)
 constexpr int ATT_SMEM = 1024 + 2 * Q_BYTES + ATT_STAGES * (K_BYTES + V_BYTES) + 512;
 constexpr uint32_t ATT_TMEM_COLS = 512;
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units: P <= 2^8
@@ -56,12 +58,14 @@ __device__ __forceinline__ void issue_s(uint32_t d, uint64_t dq, uint64_t dk) {
   for (int k = 0; k < 4; ++k) umma_ss(d, dq + 2 * k, dk + 2 * k, IDESC_S, k > 0 ? 1u : 0u);
 }
 
-// O (+)= P V: P (fp16, 128 keys = 64 TMEM columns) from TMEM, V^T from smem
+// O (+)= P V: P (fp16, 128 keys = 64 TMEM columns) from TMEM, V (fp16, key
+// rows of 64 values) from smem as an MN-major operand: K step kk = keys
+// 16 kk .. 16 kk + 15 starts 16 rows x 128 B = 2048 B further
 __device__ __forceinline__ void issue_pv(uint32_t d, uint32_t p_tmem, uint64_t dv, bool accumulate) {
-  constexpr uint32_t IDESC_O = idesc_f16_f32(128, HDIM);
+  constexpr uint32_t IDESC_O = idesc_f16_f32(128, HDIM) | IDESC_B_MN_MAJOR;
 #pragma unroll
   for (int kk = 0; kk < 8; ++kk)
-    umma_ts(d, p_tmem + kk * 8, dv + (kk >> 2) * ((V_BYTES / 2) >> 4) + (kk & 3) * 2, IDESC_O,
+    umma_ts(d, p_tmem + kk * 8, dv + static_cast<uint64_t>(kk * (2048 >> 4)), IDESC_O,
             (accumulate || kk > 0) ? 1u : 0u);
 }
 
@@ -188,8 +192,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
           mbar_arrive_expect_tx(&kv_full[stage], K_BYTES + V_BYTES);
           const int key0 = tile.seq_start + j * 128;
           tma_load_2d(sK + stage * K_BYTES, &tmK, &kv_full[stage], head * HDIM, key0);
-          tma_load_2d(sV + stage * V_BYTES, &tmV, &kv_full[stage], key0, head * VT_ROWS);
-          tma_load_2d(sV + stage * V_BYTES + V_BYTES / 2, &tmV, &kv_full[stage], key0 + 64, head * VT_ROWS);
+          tma_load_2d(sV + stage * V_BYTES, &tmV, &kv_full[stage], head * HDIM, key0);
           if (++stage == ATT_STAGES) {
             stage = 0;
             phase ^= 1u;
@@ -202,7 +205,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         const int i = warp - 1;
         const uint64_t dq = sdesc_sw128(smem_u32(sQ + i * Q_BYTES));
         const uint64_t dk0 = sdesc_sw128(smem_u32(sK));
-        const uint64_t dv0 = sdesc_sw128(smem_u32(sV));
+        const uint64_t dv0 = sdesc_sw128_mn(smem_u32(sV));
         const uint32_t s_t = tmem_base + s_col(i);
         const uint32_t p_t = tmem_base + p_col(i);
         const uint32_t o_t = tmem_base + o_col(i);
@@ -409,7 +412,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
 
 }  // namespace
 
-void attention(const CUtensorMap& Q, const CUtensorMap& K, const CUtensorMap& Vt, const AttnTile* tiles,
+void attention(const CUtensorMap& Q, const CUtensorMap& K, const CUtensorMap& V, const AttnTile* tiles,
                int n_tiles, int chunk, bf16* out, int* err, cudaStream_t s) {
   if (n_tiles <= 0) return;
   static bool attr_done[64] = {false};
@@ -420,7 +423,7 @@ void attention(const CUtensorMap& Q, const CUtensorMap& K, const CUtensorMap& Vt
     attr_done[dev & 63] = true;
   }
   dim3 grid(n_tiles, HEADS);
-  k_attention<<<grid, ATT_THREADS, ATT_SMEM, s>>>(Q, K, Vt, tiles, chunk, out, err);
+  k_attention<<<grid, ATT_THREADS, ATT_SMEM, s>>>(Q, K, V, tiles, chunk, out, err);
 }
 
 }  // namespace lx

@@ -201,6 +201,20 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr) {
          (static_cast<uint64_t>(2) << 61);
 }
 
+// Shared-memory matrix descriptor, MN-major operand in the 128-byte swizzle
+// layout written by a TMA load with a 64-element (128-byte) inner box along
+// MN: each K row is 128 contiguous bytes of 64 MN elements, 8-row atoms 1024
+// bytes apart (SBO = 1024).  LBO (the stride between 64-element MN groups) is
+// not used by a 64-wide operand.  Advancing K by 16 rows adds 2048 bytes.
+__device__ __forceinline__ uint64_t sdesc_sw128_mn(uint32_t saddr) {
+  return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (static_cast<uint64_t>(1024 >> 4) << 16) |
+         (static_cast<uint64_t>(1024 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) |
+         (static_cast<uint64_t>(2) << 61);
+}
+
+// Instruction-descriptor bit selecting an MN-major B operand.
+constexpr uint32_t IDESC_B_MN_MAJOR = 1u << 16;
+
 // Instruction descriptor, kind::f16 with bf16 A/B, f32 D, both K-major.
 __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
   return (1u << 4)                                   // D format f32
@@ -213,6 +227,27 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N) {
 // Instruction descriptor, kind::f16 with f16 A/B, f32 D, both K-major.
 __host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
   return (1u << 4) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+// ---------------------------------------------------------------------------
+// 256-bit global stores: one full 32-byte sector per thread (the GEMM
+// epilogues write rows per thread, so a warp store touches 32 rows; a 16-byte
+// store would leave every sector half written by each instruction).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void st_global_v8(void* p, uint32_t a, uint32_t b, uint32_t c, uint32_t d, uint32_t e,
+                                             uint32_t f, uint32_t g, uint32_t h) {
+  asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(a), "r"(b), "r"(c), "r"(d), "r"(e),
+               "r"(f), "r"(g), "r"(h)
+               : "memory");
+}
+
+// 16 fp32 values to 64 contiguous bytes (32-byte aligned).
+__device__ __forceinline__ void store_f32x16(float* dst, const float (&v)[16]) {
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+    st_global_v8(dst + 8 * h, __float_as_uint(v[8 * h + 0]), __float_as_uint(v[8 * h + 1]),
+                 __float_as_uint(v[8 * h + 2]), __float_as_uint(v[8 * h + 3]), __float_as_uint(v[8 * h + 4]),
+                 __float_as_uint(v[8 * h + 5]), __float_as_uint(v[8 * h + 6]), __float_as_uint(v[8 * h + 7]));
 }
 
 // ---------------------------------------------------------------------------

@@ -4,7 +4,7 @@
 // a CUDA graph covering every Euler step):
 //   in_proj GEMM (x part, K=80) + per-utterance constant -> x, conv staging
 //   conv-pos 1 (Mish) -> conv-pos 2 (Mish, + residual) -> x
-//   22 x { AdaLN-mod -> QKV GEMM (+bias, partial rotary, V^T) -> flash attention
+//   22 x { AdaLN-mod -> QKV GEMM (+bias, partial rotary, fp16 V) -> flash attention
 //          -> out GEMM (+bias, gate, residual) -> AdaLN-mod
 //          -> FF1 GEMM (+bias, GELU-tanh) -> FF2 GEMM (+bias, gate, residual) }
 //   final AdaLN-mod -> proj_out GEMM (N=80) -> CFG Euler update
@@ -414,7 +414,6 @@ Plan make_plan(int n_utt, const int32_t* lengths, bool cfg_pairs, int chunk, int
     sr += L;
   }
   p.R = std::max(r, 1);
-  p.Rv = (p.R + 7) / 8 * 8;
   p.Rs = std::max(sr, 1);
   p.pos.assign(p.R, 0);
   p.p2s.assign(p.R, -1);
@@ -459,7 +458,7 @@ int ensure_workspace(lx_flow* h, const Plan& p, size_t in_floats, int n_utt) {
   if (grow) {
     clear_graphs(h);
     void** ptrs[] = {(void**)&w.x,       (void**)&w.xn,        (void**)&w.q,        (void**)&w.k,
-                     (void**)&w.vt,      (void**)&w.ao,        (void**)&w.h,        (void**)&w.stage1,
+                     (void**)&w.v,       (void**)&w.ao,        (void**)&w.h,        (void**)&w.stage1,
                      (void**)&w.stage2,  (void**)&w.cst,       (void**)&w.a_cond,   (void**)&w.xb,
                      (void**)&w.dphi,    (void**)&w.xs,        (void**)&w.pos,      (void**)&w.p2s,
                      (void**)&w.s2p,     (void**)&w.frame_utt, (void**)&w.seq_rows, (void**)&w.frame_rows,
@@ -475,11 +474,10 @@ int ensure_workspace(lx_flow* h, const Plan& p, size_t in_floats, int n_utt) {
     w.capIn = std::max(in_floats, w.capIn) + 256 * MEL;
     w.capUtt = std::max(static_cast<size_t>(n_utt), w.capUtt) + 16;
     const size_t R = w.capR, Rs = w.capRs, F = w.capF;
-    w.Rv = static_cast<int>((R + 7) / 8 * 8);
     int rc;
     if ((rc = dev_alloc(h, &w.x, R * DIM, false)) || (rc = dev_alloc(h, &w.xn, R * DIM, false)) ||
         (rc = dev_alloc(h, &w.q, R * DIM, false)) || (rc = dev_alloc(h, &w.k, R * DIM, false)) ||
-        (rc = dev_alloc(h, &w.vt, static_cast<size_t>(HEADS) * VT_ROWS * w.Rv, false)) ||
+        (rc = dev_alloc(h, &w.v, R * DIM, false)) ||
         (rc = dev_alloc(h, &w.ao, R * DIM, false)) || (rc = dev_alloc(h, &w.h, R * FF, false)) ||
         (rc = dev_alloc(h, &w.stage1, Rs * DIM, false)) || (rc = dev_alloc(h, &w.stage2, Rs * DIM, false)) ||
         (rc = dev_alloc(h, &w.cst, R * DIM, false)) || (rc = dev_alloc(h, &w.a_cond, R * COND_K, false)) ||
@@ -494,12 +492,12 @@ int ensure_workspace(lx_flow* h, const Plan& p, size_t in_floats, int n_utt) {
         (rc = dev_alloc(h, &w.in_spks, w.capUtt * MEL, false)))
       return rc;
     // every buffer starts finite: rows that no kernel writes (alignment gaps,
-    // V^T columns past the last row, staging gap rows) are read as operands
+    // rows past the last sequence, staging gap rows) are read as operands
     CK(cudaMemset(w.x, 0, R * DIM * 4));
     CK(cudaMemset(w.xn, 0, R * DIM * 2));
     CK(cudaMemset(w.q, 0, R * DIM * 2));
     CK(cudaMemset(w.k, 0, R * DIM * 2));
-    CK(cudaMemset(w.vt, 0, static_cast<size_t>(HEADS) * VT_ROWS * w.Rv * 2));
+    CK(cudaMemset(w.v, 0, R * DIM * 2));
     CK(cudaMemset(w.ao, 0, R * DIM * 2));
     CK(cudaMemset(w.h, 0, R * FF * 2));
     CK(cudaMemset(w.stage1, 0, Rs * DIM * 2));
@@ -515,7 +513,7 @@ int ensure_workspace(lx_flow* h, const Plan& p, size_t in_floats, int n_utt) {
     ok &= tmap_bf16(&w.tm_stage2, w.stage2, Rs, DIM, DIM, 128, 64);
     ok &= tmap_bf16(&w.tm_q, w.q, R, DIM, DIM, 128, 64);
     ok &= tmap_bf16(&w.tm_k, w.k, R, DIM, DIM, 128, 64);
-    ok &= tmap_bf16(&w.tm_vt, w.vt, static_cast<uint64_t>(HEADS) * VT_ROWS, w.Rv, w.Rv, VT_ROWS, 64);
+    ok &= tmap_bf16(&w.tm_v, w.v, R, DIM, DIM, 128, 64);
     ok &= tmap_f32(&w.tm_x, w.x, R, DIM, DIM, 128, 32);
     if (!ok) return h->fail(LX_ERR_CUDA, "cuTensorMapEncodeTiled failed for a workspace tensor");
     ++w.generation;
@@ -582,6 +580,7 @@ void enqueue_dit(lx_flow* h, const Plan& p, const float* mod, const float* mod_f
   const int R = p.R;
   const int bn1024 = pick_bn(R, DIM), bnq = pick_bn(R, QKV_N), bnf = pick_bn(R, FF);
   const int i1024 = bn1024 == 256, iq = bnq == 256, iff = bnf == 256;
+  const bool pair_q = use_pair_gemm(R, QKV_N), pair_f = use_pair_gemm(R, FF), pair_d = use_pair_gemm(R, DIM);
   int* err = h->d_err;
   timed(h, K_INPROJ, s, [&] { gemm_in_proj(bn1024, w.tm_xb, W.tm_winx[i1024], R, w.cst, w.x, w.stage1, w.p2s, err, s); });
   timed(h, K_CONV, s, [&] { conv_pos(w.tm_stage1, W.tm_wconv[0], p.Rs, W.bconv[0], 0, w.stage2, w.x, w.s2p, err, s); });
@@ -596,21 +595,37 @@ void enqueue_dit(lx_flow* h, const Plan& p, const float* mod, const float* mod_f
     const float* m = mod + static_cast<size_t>(l) * MOD_N;
     timed(h, K_ADALN, s, [&] { adaln_rows(w.x, w.xn, m + 0 * DIM, m + 1 * DIM, R, s); });
     timed(h, K_QKV, s, [&] {
-      gemm_qkv(bnq, w.tm_xn, W.tm_wqkv[iq], R, l * QKV_N, W.bqkv + static_cast<size_t>(l) * QKV_N, w.q, w.k, w.vt,
-               w.Rv, w.pos, W.rope, err, s);
+      if (pair_q)
+        gemm_pair_qkv(w.tm_xn, W.tm_wqkv[0], R, l * QKV_N, W.bqkv + static_cast<size_t>(l) * QKV_N, w.q, w.k, w.v,
+                      w.pos, W.rope, err, s);
+      else
+        gemm_qkv(bnq, w.tm_xn, W.tm_wqkv[iq], R, l * QKV_N, W.bqkv + static_cast<size_t>(l) * QKV_N, w.q, w.k, w.v,
+                 w.pos, W.rope, err, s);
     });
     timed(h, K_ATTN, s,
-          [&] { attention(w.tm_q, w.tm_k, w.tm_vt, w.tiles, static_cast<int>(p.tiles.size()), chunk, w.ao, err, s); });
+          [&] { attention(w.tm_q, w.tm_k, w.tm_v, w.tiles, static_cast<int>(p.tiles.size()), chunk, w.ao, err, s); });
     timed(h, K_OUT, s, [&] {
-      gemm_gate_res_tma(w.tm_ao, W.tm_wo[0], w.tm_x, R, DIM, l * DIM, W.bo + static_cast<size_t>(l) * DIM,
-                        m + 2 * DIM, w.x, err, s);
+      if (pair_d)
+        gemm_pair_gate_res(w.tm_ao, W.tm_wo[0], w.tm_x, R, DIM, l * DIM, W.bo + static_cast<size_t>(l) * DIM,
+                           m + 2 * DIM, w.x, err, s);
+      else
+        gemm_gate_res_tma(w.tm_ao, W.tm_wo[0], w.tm_x, R, DIM, l * DIM, W.bo + static_cast<size_t>(l) * DIM,
+                          m + 2 * DIM, w.x, err, s);
     });
     timed(h, K_ADALN, s, [&] { adaln_rows(w.x, w.xn, m + 3 * DIM, m + 4 * DIM, R, s); });
-    timed(h, K_FF1, s,
-          [&] { gemm_gelu(bnf, w.tm_xn, W.tm_w1[iff], R, l * FF, W.b1 + static_cast<size_t>(l) * FF, w.h, err, s); });
+    timed(h, K_FF1, s, [&] {
+      if (pair_f)
+        gemm_pair_gelu(w.tm_xn, W.tm_w1[0], R, l * FF, W.b1 + static_cast<size_t>(l) * FF, w.h, err, s);
+      else
+        gemm_gelu(bnf, w.tm_xn, W.tm_w1[iff], R, l * FF, W.b1 + static_cast<size_t>(l) * FF, w.h, err, s);
+    });
     timed(h, K_FF2, s, [&] {
-      gemm_gate_res_tma(w.tm_h, W.tm_w2[0], w.tm_x, R, FF, l * DIM, W.b2 + static_cast<size_t>(l) * DIM,
-                        m + 5 * DIM, w.x, err, s);
+      if (pair_d)
+        gemm_pair_gate_res(w.tm_h, W.tm_w2[0], w.tm_x, R, FF, l * DIM, W.b2 + static_cast<size_t>(l) * DIM,
+                           m + 5 * DIM, w.x, err, s);
+      else
+        gemm_gate_res_tma(w.tm_h, W.tm_w2[0], w.tm_x, R, FF, l * DIM, W.b2 + static_cast<size_t>(l) * DIM,
+                          m + 5 * DIM, w.x, err, s);
     });
     h->launches += 7;
     if (cap && cap->block && cap->block_index == l) {
@@ -772,7 +787,7 @@ void lx_flow_destroy(lx_flow* h) {
   cudaStreamSynchronize(h->stream);
   clear_graphs(h);
   Workspace& w = h->ws;
-  void* ws_ptrs[] = {w.x,        w.xn,       w.q,          w.k,         w.vt,        w.ao,       w.h,
+  void* ws_ptrs[] = {w.x,        w.xn,       w.q,          w.k,         w.v,        w.ao,       w.h,
                      w.stage1,   w.stage2,   w.cst,        w.a_cond,    w.xb,        w.dphi,     w.xs,
                      w.pos,      w.p2s,      w.s2p,        w.frame_utt, w.seq_rows,  w.frame_rows, w.frame_src,
                      w.tiles,    w.in_mu,    w.in_cond,    w.in_noise,  w.out_mel,   w.in_spks,  w.cap,

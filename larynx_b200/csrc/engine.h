@@ -14,7 +14,7 @@ namespace lx {
 constexpr int N_STEPS_DEFAULT = 10;
 constexpr float CFG_RATE = 0.7f;
 constexpr int ROPE_MAX = 16384;      // positions covered by the rotary table
-constexpr int SEQ_ALIGN = 8;         // packed sequences start on 8-row boundaries (TMA x alignment of V^T)
+constexpr int SEQ_ALIGN = 8;         // packed sequences start on 8-row boundaries (as lx_flow_op_attention)
 constexpr int STAGE_GAP = 32;        // zero rows before each sequence in the conv staging layout (>= k-1 = 30)
 constexpr int MAX_STEPS = 64;
 
@@ -51,7 +51,7 @@ struct Model {
 struct Plan {
   int n_seq = 0;
   std::vector<int> seq_len, seq_start, seq_sstart;
-  int R = 0, Rv = 0, Rs = 0, F = 0;
+  int R = 0, Rs = 0, F = 0;
   std::vector<int> pos, p2s, s2p, frame_utt;
   std::vector<int2> frame_rows, frame_src;
   std::vector<AttnTile> tiles;
@@ -64,7 +64,7 @@ struct Workspace {
   size_t capIn = 0, capUtt = 0;
   float* x = nullptr;
   bf16 *xn = nullptr, *q = nullptr, *k = nullptr, *ao = nullptr, *h = nullptr;
-  __half* vt = nullptr;  // [1024][Rv] fp16
+  __half* v = nullptr;   // [R][1024] fp16 (attention values)
   bf16 *stage1 = nullptr, *stage2 = nullptr;
   float* cst = nullptr;
   bf16* a_cond = nullptr;
@@ -77,8 +77,7 @@ struct Workspace {
   float *in_mu = nullptr, *in_cond = nullptr, *in_noise = nullptr, *out_mel = nullptr, *in_spks = nullptr;
   float* cap = nullptr;  // capture scratch [R][1024]
   size_t capCap = 0;
-  int Rv = 0;
-  CUtensorMap tm_xn, tm_ao, tm_h, tm_xb, tm_acond, tm_stage1, tm_stage2, tm_q, tm_k, tm_vt;
+  CUtensorMap tm_xn, tm_ao, tm_h, tm_xb, tm_acond, tm_stage1, tm_stage2, tm_q, tm_k, tm_v;
   CUtensorMap tm_x;  // fp32 residual stream, box 128 x 32
   uint64_t generation = 0;
 };

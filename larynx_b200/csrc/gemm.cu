@@ -1,9 +1,11 @@
 // tcgen05 GEMM instantiations with the Flow-specific fused epilogues, the
 // causal grouped conv-pos kernel, and tensor-map creation.
 #include <cstdio>
+#include <cstdlib>
 #include <mutex>
 
 #include "gemm.cuh"
+#include "gemm2.cuh"
 #include "kernels.h"
 
 namespace lx {
@@ -76,18 +78,17 @@ bool tmap_bf16(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, u
 // ---------------------------------------------------------------------------
 // epilogues: called per (row, 16 consecutive columns) with fp32 accumulators
 // ---------------------------------------------------------------------------
+// 16 values to 32 contiguous bytes (32-byte aligned) of bf16 / fp16.
 __device__ __forceinline__ void store_bf16x16(bf16* dst, const float (&v)[16]) {
-  uint4 a, b;
-  a.x = pack_bf16x2(v[0], v[1]);
-  a.y = pack_bf16x2(v[2], v[3]);
-  a.z = pack_bf16x2(v[4], v[5]);
-  a.w = pack_bf16x2(v[6], v[7]);
-  b.x = pack_bf16x2(v[8], v[9]);
-  b.y = pack_bf16x2(v[10], v[11]);
-  b.z = pack_bf16x2(v[12], v[13]);
-  b.w = pack_bf16x2(v[14], v[15]);
-  reinterpret_cast<uint4*>(dst)[0] = a;
-  reinterpret_cast<uint4*>(dst)[1] = b;
+  st_global_v8(dst, pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
+               pack_bf16x2(v[6], v[7]), pack_bf16x2(v[8], v[9]), pack_bf16x2(v[10], v[11]),
+               pack_bf16x2(v[12], v[13]), pack_bf16x2(v[14], v[15]));
+}
+
+__device__ __forceinline__ void store_f16x16(__half* dst, const float (&v)[16]) {
+  st_global_v8(dst, pack_f16x2(v[0], v[1]), pack_f16x2(v[2], v[3]), pack_f16x2(v[4], v[5]), pack_f16x2(v[6], v[7]),
+               pack_f16x2(v[8], v[9]), pack_f16x2(v[10], v[11]), pack_f16x2(v[12], v[13]),
+               pack_f16x2(v[14], v[15]));
 }
 
 __device__ __forceinline__ void add_bias16(float (&v)[16], const float* bias) {
@@ -106,12 +107,11 @@ struct EpiQKV {
   const float* bias;
   bf16* q;
   bf16* k;
-  __half* vt;  // V^T in fp16: the B operand of the attention PV MMA
-  int ldvt;
+  __half* v;  // fp16 [M][1024]: the MN-major B operand of the attention PV MMA
   const int* pos;
   const float2* rope;  // [pos][32] (cos, sin)
-  __device__ __forceinline__ void operator()(int row, int col0, float (&v)[16]) const {
-    add_bias16(v, bias + col0);
+  __device__ __forceinline__ void operator()(int row, int col0, float (&v16)[16]) const {
+    add_bias16(v16, bias + col0);
     const int which = col0 >> 10;
     const int c = col0 & (DIM - 1);
     if (which < 2) {
@@ -121,16 +121,14 @@ struct EpiQKV {
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const float2 t = __ldg(cs + i);
-          const float x0 = v[2 * i], x1 = v[2 * i + 1];
-          v[2 * i] = x0 * t.x - x1 * t.y;
-          v[2 * i + 1] = x1 * t.x + x0 * t.y;
+          const float x0 = v16[2 * i], x1 = v16[2 * i + 1];
+          v16[2 * i] = x0 * t.x - x1 * t.y;
+          v16[2 * i + 1] = x1 * t.x + x0 * t.y;
         }
       }
-      store_bf16x16((which == 0 ? q : k) + static_cast<size_t>(row) * DIM + c, v);
+      store_bf16x16((which == 0 ? q : k) + static_cast<size_t>(row) * DIM + c, v16);
     } else {
-      __half* dst = vt + static_cast<size_t>((c >> 6) * VT_ROWS + (c & 63)) * ldvt + row;
-#pragma unroll
-      for (int j = 0; j < 16; ++j) dst[static_cast<size_t>(j) * ldvt] = __float2half_rn(v[j]);
+      store_f16x16(v + static_cast<size_t>(row) * DIM + c, v16);
     }
   }
 };
@@ -140,20 +138,22 @@ struct EpiGateRes {
   const float* gate;
   float* x;
   __device__ __forceinline__ void operator()(int row, int col0, float (&v)[16]) const {
-    float4* xr = reinterpret_cast<float4*>(x + static_cast<size_t>(row) * DIM + col0);
+    float* xr = x + static_cast<size_t>(row) * DIM + col0;
+    const float4* x4 = reinterpret_cast<const float4*>(xr);
     const float4* b4 = reinterpret_cast<const float4*>(bias + col0);
     const float4* g4 = reinterpret_cast<const float4*>(gate + col0);
+    float o[16];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      float4 xv = xr[j];
+      const float4 xv = x4[j];
       const float4 b = __ldg(b4 + j);
       const float4 g = __ldg(g4 + j);
-      xv.x += g.x * (v[4 * j + 0] + b.x);
-      xv.y += g.y * (v[4 * j + 1] + b.y);
-      xv.z += g.z * (v[4 * j + 2] + b.z);
-      xv.w += g.w * (v[4 * j + 3] + b.w);
-      xr[j] = xv;
+      o[4 * j + 0] = xv.x + g.x * (v[4 * j + 0] + b.x);
+      o[4 * j + 1] = xv.y + g.y * (v[4 * j + 1] + b.y);
+      o[4 * j + 2] = xv.z + g.z * (v[4 * j + 2] + b.z);
+      o[4 * j + 3] = xv.w + g.w * (v[4 * j + 3] + b.w);
     }
+    store_f32x16(xr, o);
   }
 };
 
@@ -164,20 +164,19 @@ struct EpiGateResSmem {
   const float* gate;
   float* x;
   __device__ __forceinline__ void operator()(int row, int col0, float (&v)[16], const float (&xin)[16]) const {
-    float4* xr = reinterpret_cast<float4*>(x + static_cast<size_t>(row) * DIM + col0);
     const float4* b4 = reinterpret_cast<const float4*>(bias + col0);
     const float4* g4 = reinterpret_cast<const float4*>(gate + col0);
+    float o[16];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const float4 b = __ldg(b4 + j);
       const float4 g = __ldg(g4 + j);
-      float4 o;
-      o.x = xin[4 * j + 0] + g.x * (v[4 * j + 0] + b.x);
-      o.y = xin[4 * j + 1] + g.y * (v[4 * j + 1] + b.y);
-      o.z = xin[4 * j + 2] + g.z * (v[4 * j + 2] + b.z);
-      o.w = xin[4 * j + 3] + g.w * (v[4 * j + 3] + b.w);
-      xr[j] = o;
+      o[4 * j + 0] = xin[4 * j + 0] + g.x * (v[4 * j + 0] + b.x);
+      o[4 * j + 1] = xin[4 * j + 1] + g.y * (v[4 * j + 1] + b.y);
+      o[4 * j + 2] = xin[4 * j + 2] + g.z * (v[4 * j + 2] + b.z);
+      o[4 * j + 3] = xin[4 * j + 3] + g.w * (v[4 * j + 3] + b.w);
     }
+    store_f32x16(x + static_cast<size_t>(row) * DIM + col0, o);
   }
 };
 
@@ -198,9 +197,7 @@ struct EpiF32 {
   int ldo;
   __device__ __forceinline__ void operator()(int row, int col0, float (&v)[16]) const {
     if (bias) add_bias16(v, bias + col0);
-    float4* o = reinterpret_cast<float4*>(out + static_cast<size_t>(row) * ldo + col0);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) o[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    store_f32x16(out + static_cast<size_t>(row) * ldo + col0, v);
   }
 };
 
@@ -211,7 +208,6 @@ struct EpiInProj {
   const int* p2s;
   __device__ __forceinline__ void operator()(int row, int col0, float (&v)[16]) const {
     const float4* c4 = reinterpret_cast<const float4*>(cst + static_cast<size_t>(row) * DIM + col0);
-    float4* xr = reinterpret_cast<float4*>(x + static_cast<size_t>(row) * DIM + col0);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const float4 c = c4[j];
@@ -219,8 +215,8 @@ struct EpiInProj {
       v[4 * j + 1] += c.y;
       v[4 * j + 2] += c.z;
       v[4 * j + 3] += c.w;
-      xr[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
     }
+    store_f32x16(x + static_cast<size_t>(row) * DIM + col0, v);
     const int srow = __ldg(p2s + row);
     if (srow >= 0) store_bf16x16(stage + static_cast<size_t>(srow) * DIM + col0, v);
   }
@@ -241,16 +237,17 @@ struct EpiConv {
     if (!second) {
       store_bf16x16(out_stage + static_cast<size_t>(srow) * DIM + col0, v);
     } else {
-      float4* xr = reinterpret_cast<float4*>(x + static_cast<size_t>(prow) * DIM + col0);
+      float* xr = x + static_cast<size_t>(prow) * DIM + col0;
+      const float4* x4 = reinterpret_cast<const float4*>(xr);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        float4 xv = xr[j];
-        xv.x += v[4 * j + 0];
-        xv.y += v[4 * j + 1];
-        xv.z += v[4 * j + 2];
-        xv.w += v[4 * j + 3];
-        xr[j] = xv;
+        const float4 xv = x4[j];
+        v[4 * j + 0] += xv.x;
+        v[4 * j + 1] += xv.y;
+        v[4 * j + 2] += xv.z;
+        v[4 * j + 3] += xv.w;
       }
+      store_f32x16(xr, v);
     }
   }
 };
@@ -277,6 +274,26 @@ static void launch(const CUtensorMap& A, const CUtensorMap& B, int M, int N, int
   k_gemm<BN, STAGES, MODE, Epi><<<grid, gemm_threads(MODE), smem, s>>>(A, B, X ? *X : A, sh, epi);
 }
 
+// CTA-pair launch: persistent grid of up to num_sms() / 2 clusters of 2.
+template <int STAGES, bool RES, int XS, class Epi>
+static void launch_pair(const CUtensorMap& A, const CUtensorMap& B, int M, int N, int K, int b_off, const Epi& epi,
+                        int* err, cudaStream_t s, const CUtensorMap* X = nullptr) {
+  constexpr int smem = gemm2_smem_bytes<STAGES, RES, XS>();
+  static bool attr_done[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_done[dev & 63]) {
+    cudaFuncSetAttribute(k_gemm2<STAGES, RES, XS, Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    attr_done[dev & 63] = true;
+  }
+  const int tiles = ((M + G2_BM - 1) / G2_BM) * (N / G2_BN);
+  int pairs = num_sms() / 2;
+  if (tiles < pairs) pairs = tiles;
+  if (pairs <= 0) return;
+  GemmShape sh{M, N, K, b_off, err};
+  k_gemm2<STAGES, RES, XS, Epi><<<2 * pairs, GEMM2_THREADS, smem, s>>>(A, B, X ? *X : A, sh, epi);
+}
+
 template <class Epi>
 static void launch_bn(int bn, const CUtensorMap& A, const CUtensorMap& B, int M, int N, int K, int b_off,
                       const Epi& e, int* err, cudaStream_t s) {
@@ -293,8 +310,8 @@ int pick_bn(int M, int N) {
 }
 
 void gemm_qkv(int bn, const CUtensorMap& A, const CUtensorMap& B, int M, int b_off, const float* bias, bf16* q,
-              bf16* k, __half* vt, int ldvt, const int* pos, const float2* rope, int* err, cudaStream_t s) {
-  EpiQKV e{bias, q, k, vt, ldvt, pos, rope};
+              bf16* k, __half* v, const int* pos, const float2* rope, int* err, cudaStream_t s) {
+  EpiQKV e{bias, q, k, v, pos, rope};
   launch_bn(bn, A, B, M, QKV_N, DIM, b_off, e, err, s);
 }
 
@@ -308,6 +325,42 @@ void gemm_gate_res_tma(const CUtensorMap& A, const CUtensorMap& B, const CUtenso
                        const float* bias, const float* gate, float* x, int* err, cudaStream_t s) {
   EpiGateResSmem e{bias, gate, x};
   launch<128, 4, MODE_RESID>(A, B, M, DIM, K, b_off, e, err, s, &X);
+}
+
+void gemm_pair_qkv(const CUtensorMap& A, const CUtensorMap& B, int M, int b_off, const float* bias, bf16* q,
+                   bf16* k, __half* v, const int* pos, const float2* rope, int* err, cudaStream_t s) {
+  EpiQKV e{bias, q, k, v, pos, rope};
+  launch_pair<6, false, 0>(A, B, M, QKV_N, DIM, b_off, e, err, s);
+}
+
+void gemm_pair_gelu(const CUtensorMap& A, const CUtensorMap& B, int M, int b_off, const float* bias, bf16* h,
+                    int* err, cudaStream_t s) {
+  EpiGelu e{bias, h};
+  launch_pair<6, false, 0>(A, B, M, FF, DIM, b_off, e, err, s);
+}
+
+void gemm_pair_gate_res(const CUtensorMap& A, const CUtensorMap& B, const CUtensorMap& X, int M, int K, int b_off,
+                        const float* bias, const float* gate, float* x, int* err, cudaStream_t s) {
+  EpiGateResSmem e{bias, gate, x};
+  launch_pair<4, true, 3>(A, B, M, DIM, K, b_off, e, err, s, &X);
+}
+
+void gemm_pair_f32(const CUtensorMap& A, const CUtensorMap& B, int M, int N, int K, const float* bias, float* out,
+                   int ldo, int* err, cudaStream_t s) {
+  EpiF32 e{bias, out, ldo};
+  launch_pair<6, false, 0>(A, B, M, N, K, 0, e, err, s);
+}
+
+bool use_pair_gemm(int M, int N) {
+  static int env = -1;
+  if (env < 0) {
+    const char* e = getenv("LX_FLOW_PAIR_GEMM");
+    env = (e && e[0] == '0') ? 0 : (e && e[0] == '2') ? 2 : 1;
+  }
+  if (!env || N % G2_BN != 0) return false;
+  if (env == 2) return true;
+  const long pair_tiles = static_cast<long>((M + G2_BM - 1) / G2_BM) * (N / G2_BN);
+  return pair_tiles >= 2L * (num_sms() / 2);
 }
 
 void gemm_gelu(int bn, const CUtensorMap& A, const CUtensorMap& B, int M, int b_off, const float* bias, bf16* h,

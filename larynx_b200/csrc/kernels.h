@@ -24,8 +24,6 @@ constexpr int MOD_N = 6 * DIM;
 constexpr int CONV_K = 31;
 constexpr int CONV_G = 16;
 constexpr int COND_K = 3 * MEL;  // [cond, mu, spks] columns of the input projection
-// V^T rows per head (value channels)
-constexpr int VT_ROWS = 64;
 
 // Number of SMs of the current device (cached per device).
 int num_sms();
@@ -54,10 +52,10 @@ struct AttnTile {
 // map's box must be bn x 64.  `b_off` selects the layer slice of stacked
 // weights (row offset into B).
 int pick_bn(int M, int N);
-// q/k [M,1024] bf16 with bias + partial rotary on channels 0..63; v written
-// transposed to vt[1024][ldvt] in fp16 (the PV operand of the attention).
+// q/k [M,1024] bf16 with bias + partial rotary on channels 0..63; v [M,1024]
+// in fp16 (the MN-major PV operand of the attention).
 void gemm_qkv(int bn, const CUtensorMap& A, const CUtensorMap& B, int M, int b_off, const float* bias, bf16* q,
-              bf16* k, __half* vt, int ldvt, const int* pos, const float2* rope, int* err, cudaStream_t s);
+              bf16* k, __half* v, const int* pos, const float2* rope, int* err, cudaStream_t s);
 // x[M,1024] += gate[col] * (A*B^T + bias), residual tile prefetched by TMA
 // through X (fp32 map of x, box 128 rows x 32 cols); B box 128 x 64.
 void gemm_gate_res_tma(const CUtensorMap& A, const CUtensorMap& B, const CUtensorMap& X, int M, int K, int b_off,
@@ -75,6 +73,20 @@ void gemm_f32(int bn, const CUtensorMap& A, const CUtensorMap& B, int M, int N, 
 // x-part of the input projection: v = A*B^T + cst; x = v; stage[p2s[row]] = bf16(v)
 void gemm_in_proj(int bn, const CUtensorMap& A, const CUtensorMap& B, int M, const float* cst, float* x,
                   bf16* stage, const int* p2s, int* err, cudaStream_t s);
+// CTA-pair (cta_group::2) forms of the QKV, FF1 and residual GEMMs: 256 x 256
+// tiles per pair of SMs; every B map has a 128 x 64 box, N % 256 == 0.
+// use_pair_gemm decides by problem size (enough tiles for two waves of pairs);
+// LX_FLOW_PAIR_GEMM=0 in the environment turns the pair path off, =2 uses it
+// at every size (parity tests of small problems).
+bool use_pair_gemm(int M, int N);
+void gemm_pair_f32(const CUtensorMap& A, const CUtensorMap& B, int M, int N, int K, const float* bias, float* out,
+                   int ldo, int* err, cudaStream_t s);
+void gemm_pair_qkv(const CUtensorMap& A, const CUtensorMap& B, int M, int b_off, const float* bias, bf16* q,
+                   bf16* k, __half* v, const int* pos, const float2* rope, int* err, cudaStream_t s);
+void gemm_pair_gelu(const CUtensorMap& A, const CUtensorMap& B, int M, int b_off, const float* bias, bf16* h,
+                    int* err, cudaStream_t s);
+void gemm_pair_gate_res(const CUtensorMap& A, const CUtensorMap& B, const CUtensorMap& X, int M, int K, int b_off,
+                        const float* bias, const float* gate, float* x, int* err, cudaStream_t s);
 // causal grouped conv (k=31, 16 groups) over the staged rows [0, Ms); B box 64 x 64.
 // second == 0: out_stage[srow] = bf16(mish(conv + bias))  (rows with s2p >= 0)
 // second == 1: x[s2p[srow]] += mish(conv + bias)
@@ -84,7 +96,8 @@ void conv_pos(const CUtensorMap& A, const CUtensorMap& B, int Ms, const float* b
 // ---- attention (tcgen05 flash attention) -----------------------------------
 // out[row, 64h..64h+63] for every valid query row of every tile; chunk > 0
 // applies the block-causal chunk mask, keys >= seq_len are always masked.
-void attention(const CUtensorMap& Q, const CUtensorMap& K, const CUtensorMap& Vt, const AttnTile* tiles,
+// Q, K: bf16 [R][1024] maps, V: fp16 [R][1024] map; all boxes 128 rows x 64.
+void attention(const CUtensorMap& Q, const CUtensorMap& K, const CUtensorMap& V, const AttnTile* tiles,
                int n_tiles, int chunk, bf16* out, int* err, cudaStream_t s);
 
 // ---- element-wise / row kernels -----------------------------------------

@@ -8,22 +8,22 @@
 // queued on other streams, and take unbounded time; an audio pipeline with a
 // per-chunk deadline, or an embedder that hands the whole of HBM to its own
 // pool allocator up front, cannot accept either.  lx_flow_op_attention
-// allocates its V^T copy, tile list and error word on every call; this entry
-// point uses fixed static storage instead.
+// allocates its fp16 copy of V, tile list and error word on every call; this
+// entry point uses fixed static storage instead.
 //
 // Limit (checked on the host; a larger call returns LX_ERR_ARG before any
 // device work is queued): packed rows R = sum_i round_up(len_i, 8) <=
 // LX_STATIC_ATT_MAX_ROWS (4096).  Query tiles = sum_i ceil(len_i / 256) <= R / 8,
-// so 512 tile slots always suffice.  The static storage is 8 MiB of V^T
-// (fp16 [1024][4096]) + 8 KiB of tiles + one error word per device.
+// so 512 tile slots always suffice.  The static storage is 8 MiB of fp16 V
+// ([4096][1024]) + 8 KiB of tiles + one error word per device.
 //
 // Set-up: the first call on a device (with that device current) resolves the
 // arrays' addresses with cudaGetSymbolAddress, which can load the module; make
 // that first call before any stream capture begins.  Later calls do no set-up.
 //
 // Zero state: only the error word must start at zero; each call clears it on
-// the caller's stream before the kernels run.  Every V^T column the attention
-// reads inside [0, R) is rewritten by the call's transpose, and keys past R
+// the caller's stream before the kernels run.  Every V row the attention
+// reads inside [0, R) is rewritten by the call's conversion, and keys past R
 // come from the tensor map's zero fill, so nothing else needs clearing.
 //
 // Concurrency: the storage is shared by every call on a device.  Calls that
@@ -44,12 +44,12 @@ constexpr int kMaxRows = LX_STATIC_ATT_MAX_ROWS;
 constexpr int kMaxTiles = kMaxRows / 8;
 constexpr int kMaxDevices = 64;
 
-__device__ __align__(256) __half g_vt[static_cast<size_t>(HEADS) * VT_ROWS * kMaxRows];
+__device__ __align__(256) __half g_v[static_cast<size_t>(kMaxRows) * DIM];
 __device__ __align__(256) AttnTile g_tiles[kMaxTiles];
 __device__ __align__(256) int g_err[1];
 
 struct Scratch {
-  __half* vt = nullptr;
+  __half* v = nullptr;
   AttnTile* tiles = nullptr;
   int* err = nullptr;
 };
@@ -65,7 +65,7 @@ int scratch_for_current_device(Scratch* out) {
   std::lock_guard<std::mutex> lock(g_setup_mu);
   if (!g_ready[dev]) {
     Scratch s;
-    if (cudaGetSymbolAddress(reinterpret_cast<void**>(&s.vt), g_vt) != cudaSuccess ||
+    if (cudaGetSymbolAddress(reinterpret_cast<void**>(&s.v), g_v) != cudaSuccess ||
         cudaGetSymbolAddress(reinterpret_cast<void**>(&s.tiles), g_tiles) != cudaSuccess ||
         cudaGetSymbolAddress(reinterpret_cast<void**>(&s.err), g_err) != cudaSuccess)
       return LX_ERR_CUDA;
@@ -76,14 +76,17 @@ int scratch_for_current_device(Scratch* out) {
   return LX_OK;
 }
 
-// v[R][1024] bf16 -> vt[(c/64)*64 + c%64][ldvt] fp16: the same layout the
-// attention kernel's PV operand tensor map describes.
-__global__ void k_transpose_v_static(const bf16* __restrict__ v, __half* __restrict__ vt, int R, int ldvt) {
-  const int r = blockIdx.x * 32 + threadIdx.x;
-  const int c = blockIdx.y * 32 + threadIdx.y;
-  if (r < R && c < DIM)
-    vt[static_cast<size_t>((c >> 6) * VT_ROWS + (c & 63)) * ldvt + r] =
-        __float2half_rn(__bfloat162float(v[static_cast<size_t>(r) * DIM + c]));
+// v[R][1024] bf16 -> fp16 in the same layout (the attention's PV operand type).
+__global__ void k_v_to_f16_static(const bf16* __restrict__ v, __half* __restrict__ vh, int n8) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n8) return;
+  const uint4 a = reinterpret_cast<const uint4*>(v)[i];
+  const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&a);
+  uint4 o;
+  __half2* h = reinterpret_cast<__half2*>(&o);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) h[j] = __float22half2_rn(__bfloat1622float2(b[j]));
+  reinterpret_cast<uint4*>(vh)[i] = o;
 }
 
 }  // namespace
@@ -105,17 +108,17 @@ extern "C" int lx_flow_op_attention_static(int n_seq, const int32_t* lengths, co
   }
   Scratch sc;
   if (int rc = scratch_for_current_device(&sc)) return rc;
-  const int rows = static_cast<int>(R);  // a multiple of 8: the V^T row stride
+  const int rows = static_cast<int>(R);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   CUtensorMap tq, tk, tv;
   if (!tmap_bf16(&tq, q, rows, DIM, DIM, 128, 64) || !tmap_bf16(&tk, k, rows, DIM, DIM, 128, 64) ||
-      !tmap_bf16(&tv, sc.vt, static_cast<uint64_t>(HEADS) * VT_ROWS, rows, rows, VT_ROWS, 64))
+      !tmap_bf16(&tv, sc.v, rows, DIM, DIM, 128, 64))
     return LX_ERR_ARG;
   if (cudaMemsetAsync(sc.err, 0, sizeof(int), s) != cudaSuccess ||
       cudaMemcpyAsync(sc.tiles, tiles, n_tiles * sizeof(AttnTile), cudaMemcpyHostToDevice, s) != cudaSuccess)
     return LX_ERR_CUDA;
-  k_transpose_v_static<<<dim3((rows + 31) / 32, DIM / 32), dim3(32, 32), 0, s>>>(static_cast<const bf16*>(v), sc.vt,
-                                                                                rows, rows);
+  const int n8 = rows * (DIM / 8);
+  k_v_to_f16_static<<<(n8 + 255) / 256, 256, 0, s>>>(static_cast<const bf16*>(v), sc.v, n8);
   attention(tq, tk, tv, sc.tiles, n_tiles, chunk, static_cast<bf16*>(out), sc.err, s);
   if (cudaGetLastError() != cudaSuccess || cudaStreamSynchronize(s) != cudaSuccess) return LX_ERR_CUDA;
   int e = 0;

@@ -211,12 +211,13 @@ class FlowDecoder:
         return out
 
     def decode_device(self, lengths: np.ndarray, mu_ptr: int, cond_ptr: int, spks_ptr: int, noise_ptr: int,
-                      out_ptr: int, chunk: int = 0, stream: int = 0) -> None:
-        """Device-pointer decode enqueued on ``stream`` (no synchronisation)."""
+                      out_ptr: int, chunk: int = 0, stream: int = 0, n_steps: int = 0) -> None:
+        """Device-pointer decode enqueued on ``stream`` (no synchronisation).
+        n_steps 0 runs the full 10-step schedule, 1..10 its first n steps."""
         L = np.ascontiguousarray(np.asarray(lengths, dtype=np.int32))
         self._dev_lengths = L  # keep alive for the call
         b = LxFlowBatch(int(L.size), L.ctypes.data_as(_i32p), mu_ptr, cond_ptr, spks_ptr, noise_ptr, out_ptr,
-                        int(chunk), 0)
+                        int(chunk), int(n_steps))
         self._raise(self._lib.lx_flow_decode_device(self._h, ctypes.byref(b), ctypes.c_void_p(stream or None)),
                     "decode_device")
 
