@@ -1,30 +1,35 @@
 // Fused flash attention for the DiT blocks on sm_100a (tcgen05 + TMEM).
 //
-// One CTA = one (sequence, 256-query block, head), head_dim = 64, processed as
-// two independent 128-row sub-tiles.  Warpgroup 0 is the producer (registers
-// lowered with setmaxnreg), warpgroups 1 and 2 run the softmax of sub-tiles 0
-// and 1 (registers raised).  Tensor memory per sub-tile i (256 columns):
-// S_i [0,128), P_i [128,192) (fp16 pairs), O_i [192,256).
-//   warp 0      TMA: both Q sub-tiles once, then per stage the K tile
-//               [128 keys x 64] (bf16) and the V tile [128 keys x 64] (fp16,
-//               row-major as the QKV GEMM wrote it; the PV MMA reads it as
-//               an MN-major operand, so no transpose exists anywhere)
-//   warp 1+i    (i = 0, 1) issues the MMAs of sub-tile i: S_i = Q_i K_j+1^T
-//               (M=128, N=128, K=64, bf16) as soon as the softmax has pulled
-//               S_i,j into registers, so QK^T of tile j+1 runs under the
-//               softmax of tile j; then O_i += P_i V_j (M=128, N=64, K=128,
-//               fp16, P read from tensor memory).  One issuing thread per
-//               sub-tile: a tcgen05.mma takes ~70 cycles to issue.
-//   warp 3      idle
-//   warps 4..7  softmax of sub-tile 0, warps 8..11 softmax of sub-tile 1:
-//               thread = query row; S row from TMEM into registers,
+// One CTA = one (128-query block, head) of one sequence, head_dim = 64; two
+// CTAs share each SM (256 threads, 128 registers per thread at launch,
+// 80 KB of shared memory and 256 tensor-memory columns each).  Two resident
+// CTAs are what keeps the MUFU units busy: while one CTA loads its scores,
+// reduces the row max, stores P or runs its prologue / epilogue, the other
+// one's exponentials run, with no hand-off between them.
+//
+// Tensor memory (256 columns): S [0,128), P [128,192) (fp16 pairs), O [192,256).
+//   warp 0      TMA: the Q tile once, then the K tiles [128 keys x 64] (bf16)
+//               through a 2-slot ring released as soon as QK^T has read them
+//   warp 2      TMA: the V tiles [128 keys x 64] (fp16, row-major as the QKV
+//               GEMM wrote it; the PV MMA reads it as an MN-major operand, so
+//               no transpose exists anywhere) through a 2-slot ring released
+//               after PV.  Separate rings keep the K load of tile j+1 off the
+//               softmax -> PV -> release chain of tile j-1.
+//   warp 1      lane 0 issues the MMAs: S = Q K_j+1^T (M=128, N=128, K=64,
+//               bf16) as soon as the softmax has pulled S_j into registers,
+//               so QK^T of tile j+1 runs under the softmax of tile j; then
+//               O += P_j V_j (M=128, N=64, K=128, fp16, P read from tensor
+//               memory)
+//   warp 3      idle (warpgroup 0 lowers its registers with setmaxnreg)
+//   warps 4..7  softmax: thread = query row; S row from TMEM into registers,
 //               key-padding / block-causal mask on boundary tiles only,
 //               online softmax in the exp2 domain (fp32 row sum), P written
 //               as packed fp16 into its own TMEM columns (P never touches
 //               shared memory, whose bandwidth the MMA operands need).  O is
 //               rescaled in place only when a row's running max grows by more
 //               than 2^8 (the reference max is otherwise kept, which is exact).
-// No score matrix ever reaches HBM.
+// The host orders the query blocks longest first, so the shortest CTAs fill
+// the last wave.  No score matrix ever reaches HBM.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -32,22 +37,23 @@ namespace lx {
 
 namespace {
 
-constexpr int ATT_THREADS = 384;  // 3 warpgroups: producer (TMA, 2 MMA, 1 idle), softmax 0, softmax 1
-// Register split with setmaxnreg: the block is launched with 384 x 168 = 64512
-// registers; producer warpgroup 128 x 56 + softmax warpgroups 256 x 224 = 64512.
-constexpr int REGS_PRODUCER = 56;
-constexpr int REGS_SOFTMAX = 224;
-constexpr int ATT_STAGES = 4;
-constexpr int Q_BYTES = 128 * 64 * 2;  // 16 KB per sub-tile
+constexpr int ATT_THREADS = 256;  // warpgroup 0: K TMA, MMA, V TMA, idle; warpgroup 1: softmax
+// Register split with setmaxnreg: the block is launched with 256 x 128 = 32768
+// registers (two blocks per SM); warpgroup 0 drops to 48, warpgroup 1 rises
+// to 208: 128 x 48 + 128 x 208 = 32768.  attention() checks the launch
+// register count before the first launch, so the raise can always be met.
+constexpr int ATT_LAUNCH_REGS = 128;
+constexpr int REGS_PRODUCER = 48;
+constexpr int REGS_SOFTMAX = 208;
+static_assert(128 * REGS_PRODUCER + 128 * REGS_SOFTMAX <= ATT_THREADS * ATT_LAUNCH_REGS, "register split");
+constexpr int ATT_STAGES = 2;
+constexpr int Q_BYTES = 128 * 64 * 2;  // 16 KB
 constexpr int K_BYTES = 128 * 64 * 2;  // 16 KB
 constexpr int V_BYTES = 128 * 64 * 2;  // 16 KB: 128 keys x 64 fp16 values (MN-major B of PV)
-constexpr int ATT_SMEM = 1024 + 2 * Q_BYTES + ATT_STAGES * (K_BYTES + V_BYTES) + 512;
-constexpr uint32_t ATT_TMEM_COLS = 512;
+constexpr int ATT_SMEM = 1024 + Q_BYTES + ATT_STAGES * (K_BYTES + V_BYTES) + 256;
+constexpr uint32_t ATT_TMEM_COLS = 256;
+constexpr uint32_t S_COL = 0, P_COL = 128, O_COL = 192;
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units: P <= 2^8
-
-__device__ __forceinline__ uint32_t s_col(int i) { return static_cast<uint32_t>(i * 256); }
-__device__ __forceinline__ uint32_t p_col(int i) { return static_cast<uint32_t>(i * 256 + 128); }
-__device__ __forceinline__ uint32_t o_col(int i) { return static_cast<uint32_t>(i * 256 + 192); }
 
 // S = Q K^T from precomputed descriptors (start address advanced by 32 B = 2
 // units per K=16 step; smem addresses stay below 2^18, so no carry leaves the
@@ -116,53 +122,98 @@ __device__ __forceinline__ void regs_inc() {
 
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-__global__ void __launch_bounds__(ATT_THREADS, 1)
+// 2^x for a pair on the FMA pipe, for x <= 8 (the lazy-rescale bound; -inf
+// allowed): x is clamped to -125 (2^-125 becomes 0 in fp16 and is negligible
+// in the fp32 row sum), split as n + f with n = round(x) by the 1.5 * 2^23
+// shifter and f in [-0.5, 0.5], 2^f from a cubic fitted to 2^f on [-0.5, 0.5]
+// for minimum maximum relative error (weighted least squares, max relative
+// error 7.5e-5, below the 4.9e-4 fp16 rounding of P), and 2^n added to the
+// exponent field.  Its use offloads part of the exponentials from the MUFU
+// units, which bound the softmax.
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  constexpr float SHIFT = 12582912.0f;  // 1.5 * 2^23
+  x.x = fmaxf(x.x, -125.0f);
+  x.y = fmaxf(x.y, -125.0f);
+  const float2 t = __fadd2_rn(x, make_float2(SHIFT, SHIFT));
+  const float2 n = __fadd2_rn(t, make_float2(-SHIFT, -SHIFT));
+  const float2 f = __fadd2_rn(x, make_float2(-n.x, -n.y));
+  float2 p = __ffma2_rn(make_float2(0.055171654f, 0.055171654f), f, make_float2(0.24261113f, 0.24261113f));
+  p = __ffma2_rn(p, f, make_float2(0.69326097f, 0.69326097f));
+  p = __ffma2_rn(p, f, make_float2(0.99992806f, 0.99992806f));
+  // low 9 bits of the shifter's bit pattern hold n (two's complement)
+  const uint32_t ex = __float_as_uint(t.x) << 23, ey = __float_as_uint(t.y) << 23;
+  return make_float2(__uint_as_float(__float_as_uint(p.x) + ex), __uint_as_float(__float_as_uint(p.y) + ey));
+}
+
+// Pairs of a 32-score chunk whose exponentials run on the FMA pipe (bit i =
+// pair i).  0: the softmax is bound by issue slots, not by the MUFU units, at
+// this head size, so every exponential stays on MUFU.
+constexpr uint32_t ATT_POLY_PAIRS = 0x0000u;
+
+// p = 2^(s * sl2 - m) for 32 scores (packed f32x2 FMA, MUFU ex2 or the FMA
+// polynomial), their fp32 sum added to (acc0, acc1), and the 32
+// probabilities packed as 16 fp16 pairs.
+__device__ __forceinline__ void exp_chunk32(const float* s, float sl2, float m, float2& acc0, float2& acc1,
+                                            uint32_t* pk) {
+  const float2 scale = make_float2(sl2, sl2);
+  const float2 neg_m = make_float2(-m, -m);
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const float2 x = __ffma2_rn(make_float2(s[2 * i], s[2 * i + 1]), scale, neg_m);
+    const float2 p = ((ATT_POLY_PAIRS >> i) & 1u) ? exp2_poly2(x) : make_float2(ex2(x.x), ex2(x.y));
+    if (i & 1)
+      acc1 = __fadd2_rn(acc1, p);
+    else
+      acc0 = __fadd2_rn(acc0, p);
+    pk[i] = pack_f16x2(p.x, p.y);
+  }
+}
+
+__global__ void __launch_bounds__(ATT_THREADS, 2)
     k_attention(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                 const __grid_constant__ CUtensorMap tmV, const AttnTile* __restrict__ tiles, int chunk,
                 bf16* __restrict__ out, int* err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;  // 2 sub-tiles
-  uint8_t* sK = sQ + 2 * Q_BYTES;
+  uint8_t* sQ = smem;
+  uint8_t* sK = sQ + Q_BYTES;
   uint8_t* sV = sK + ATT_STAGES * K_BYTES;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sV + ATT_STAGES * V_BYTES);
   uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;
-  uint64_t* kv_empty = kv_full + ATT_STAGES;
-  uint64_t* s_full = kv_empty + ATT_STAGES;  // [2]
-  uint64_t* s_empty = s_full + 2;            // [2]
-  uint64_t* p_full = s_empty + 2;            // [2]
-  uint64_t* o_done = p_full + 2;             // [2]
-  uint64_t* turn = o_done + 2;               // [2] exp-phase token between the softmax warpgroups
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(turn + 2);
+  uint64_t* k_full = bars + 1;
+  uint64_t* k_empty = k_full + ATT_STAGES;
+  uint64_t* v_full = k_empty + ATT_STAGES;
+  uint64_t* v_empty = v_full + ATT_STAGES;
+  uint64_t* s_full = v_empty + ATT_STAGES;
+  uint64_t* s_empty = s_full + 1;
+  uint64_t* p_full = s_empty + 1;
+  uint64_t* o_done = p_full + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const AttnTile tile = tiles[blockIdx.x];
-  const int head = blockIdx.y;
+  const int head = blockIdx.x;
+  const AttnTile tile = tiles[blockIdx.y];
   const int len = tile.seq_len;
-  const int nq0 = max(0, min(128, len - tile.q0));
-  const int nq1 = max(0, min(128, len - tile.q0 - 128));
-  const int n_sub = nq1 > 0 ? 2 : 1;
+  const int nq = min(128, len - tile.q0);
   // keys visible to the last query of the block
   int kv_end = len;
-  if (chunk > 0) kv_end = min(len, ((tile.q0 + nq0 + nq1 - 1) / chunk + 1) * chunk);
+  if (chunk > 0) kv_end = min(len, ((tile.q0 + nq - 1) / chunk + 1) * chunk);
   const int nkv = (kv_end + 127) / 128;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int s = 0; s < ATT_STAGES; ++s) {
-      mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], n_sub);  // one commit per sub-tile's MMA thread
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], 4);
-      mbar_init(&p_full[i], 4);
-      mbar_init(&o_done[i], 1);
-      mbar_init(&turn[i], 4);
-    }
+    mbar_init(s_full, 1);
+    mbar_init(s_empty, 4);
+    mbar_init(p_full, 4);
+    mbar_init(o_done, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -182,39 +233,49 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         tma_prefetch_desc(&tmQ);
         tma_prefetch_desc(&tmK);
         tma_prefetch_desc(&tmV);
-        mbar_arrive_expect_tx(q_full, Q_BYTES * n_sub);
-        for (int i = 0; i < n_sub; ++i)
-          tma_load_2d(sQ + i * Q_BYTES, &tmQ, q_full, head * HDIM, tile.seq_start + tile.q0 + 128 * i);
+        mbar_arrive_expect_tx(q_full, Q_BYTES);
+        tma_load_2d(sQ, &tmQ, q_full, head * HDIM, tile.seq_start + tile.q0);
         int stage = 0;
         uint32_t phase = 0;
         for (int j = 0; j < nkv; ++j) {
-          if (!mbar_wait(&kv_empty[stage], phase ^ 1u, err, abort_flag, DEV_TIMEOUT_PRODUCER)) break;
-          mbar_arrive_expect_tx(&kv_full[stage], K_BYTES + V_BYTES);
-          const int key0 = tile.seq_start + j * 128;
-          tma_load_2d(sK + stage * K_BYTES, &tmK, &kv_full[stage], head * HDIM, key0);
-          tma_load_2d(sV + stage * V_BYTES, &tmV, &kv_full[stage], head * HDIM, key0);
+          if (!mbar_wait(&k_empty[stage], phase ^ 1u, err, abort_flag, DEV_TIMEOUT_PRODUCER)) break;
+          mbar_arrive_expect_tx(&k_full[stage], K_BYTES);
+          tma_load_2d(sK + stage * K_BYTES, &tmK, &k_full[stage], head * HDIM, tile.seq_start + j * 128);
           if (++stage == ATT_STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
       }
-    } else if (warp <= 2 && warp - 1 < n_sub) {
+    } else if (warp == 2) {
       if (lane == 0) {
-        // MMA issue for sub-tile i: S_{j+1} as soon as S_j is in registers, then PV_j
-        const int i = warp - 1;
-        const uint64_t dq = sdesc_sw128(smem_u32(sQ + i * Q_BYTES));
+        int stage = 0;
+        uint32_t phase = 0;
+        for (int j = 0; j < nkv; ++j) {
+          if (!mbar_wait(&v_empty[stage], phase ^ 1u, err, abort_flag, DEV_TIMEOUT_PRODUCER)) break;
+          mbar_arrive_expect_tx(&v_full[stage], V_BYTES);
+          tma_load_2d(sV + stage * V_BYTES, &tmV, &v_full[stage], head * HDIM, tile.seq_start + j * 128);
+          if (++stage == ATT_STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    } else if (warp == 1) {
+      if (lane == 0) {
+        const uint64_t dq = sdesc_sw128(smem_u32(sQ));
         const uint64_t dk0 = sdesc_sw128(smem_u32(sK));
         const uint64_t dv0 = sdesc_sw128_mn(smem_u32(sV));
-        const uint32_t s_t = tmem_base + s_col(i);
-        const uint32_t p_t = tmem_base + p_col(i);
-        const uint32_t o_t = tmem_base + o_col(i);
+        const uint32_t s_t = tmem_base + S_COL;
+        const uint32_t p_t = tmem_base + P_COL;
+        const uint32_t o_t = tmem_base + O_COL;
         bool ok = mbar_wait(q_full, 0, err, abort_flag, DEV_TIMEOUT_MMA);
-        if (ok) ok = mbar_wait(&kv_full[0], 0, err, abort_flag, DEV_TIMEOUT_MMA);
+        if (ok) ok = mbar_wait(&k_full[0], 0, err, abort_flag, DEV_TIMEOUT_MMA);
         if (ok) {
           tc_fence_after();
           issue_s(s_t, dq, dk0);
-          umma_commit(&s_full[i]);
+          umma_commit(s_full);
+          umma_commit(&k_empty[0]);
         }
         int stage = 0;
         uint32_t phase = 0;
@@ -226,19 +287,21 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
             ph_n ^= 1u;
           }
           if (j + 1 < nkv) {
-            ok = mbar_wait(&kv_full[st_n], ph_n, err, abort_flag, DEV_TIMEOUT_MMA);
-            if (ok) ok = mbar_wait(&s_empty[i], static_cast<uint32_t>(j & 1), err, abort_flag, DEV_TIMEOUT_MMA);
+            ok = mbar_wait(&k_full[st_n], ph_n, err, abort_flag, DEV_TIMEOUT_MMA);
+            if (ok) ok = mbar_wait(s_empty, static_cast<uint32_t>(j & 1), err, abort_flag, DEV_TIMEOUT_MMA);
             if (!ok) break;
             tc_fence_after();
             issue_s(s_t, dq, dk0 + static_cast<uint64_t>((st_n * K_BYTES) >> 4));
-            umma_commit(&s_full[i]);
+            umma_commit(s_full);
+            umma_commit(&k_empty[st_n]);
           }
-          ok = mbar_wait(&p_full[i], static_cast<uint32_t>(j & 1), err, abort_flag, DEV_TIMEOUT_MMA);
+          ok = mbar_wait(p_full, static_cast<uint32_t>(j & 1), err, abort_flag, DEV_TIMEOUT_MMA);
+          if (ok) ok = mbar_wait(&v_full[stage], phase, err, abort_flag, DEV_TIMEOUT_MMA);
           if (!ok) break;
           tc_fence_after();
           issue_pv(o_t, p_t, dv0 + static_cast<uint64_t>((stage * V_BYTES) >> 4), j > 0);
-          umma_commit(&o_done[i]);
-          umma_commit(&kv_empty[stage]);
+          umma_commit(o_done);
+          umma_commit(&v_empty[stage]);
           stage = st_n;
           phase = ph_n;
         }
@@ -246,19 +309,17 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     }
   } else {
     regs_inc<REGS_SOFTMAX>();
-    // softmax warpgroup `sub` (warps 4..7 -> sub-tile 0, warps 8..11 -> sub-tile 1)
-    const int sub = (warp >> 2) - 1;
     const int q = warp & 3;       // TMEM lane quarter
-    const int r = q * 32 + lane;  // row inside the sub-tile
-    const int qi = tile.q0 + sub * 128 + r;
+    const int r = q * 32 + lane;  // row inside the query block
+    const int qi = tile.q0 + r;
     const int q_chunk = chunk > 0 ? qi / chunk : 0;
     const float sl2 = 0.125f * 1.4426950408889634f;  // 1/sqrt(64) * log2(e)
     const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
     float m_ref = -INFINITY;  // reference max, scaled (log2) units
     float l = 0.f;            // row sum of P relative to m_ref
-    bool ok = sub < n_sub;
+    bool ok = true;
     for (int j = 0; ok && j < nkv; ++j) {
-      ok = mbar_wait(&s_full[sub], static_cast<uint32_t>(j & 1), err, abort_flag, DEV_TIMEOUT_SOFTMAX);
+      ok = mbar_wait(s_full, static_cast<uint32_t>(j & 1), err, abort_flag, DEV_TIMEOUT_SOFTMAX);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
@@ -266,7 +327,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         float t[32];
-        tmem_ld32(t_lane + s_col(sub) + c * 32, t);
+        tmem_ld32(t_lane + S_COL + c * 32, t);
 #pragma unroll
         for (int i = 0; i < 32; ++i) s[c * 32 + i] = t[i];
       }
@@ -274,7 +335,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       // the S columns may now be overwritten by the next QK^T
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&s_empty[sub]);
+      if (lane == 0) mbar_arrive(s_empty);
 
       // visible keys of this row form a prefix of the tile (key padding and the
       // block-causal rule both cut at an upper bound): mask past it
@@ -303,7 +364,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         const float alpha = need ? ex2(m_ref - new_ref) : 1.0f;  // 0 from -inf
         if (j > 0) {
           // PV_{j-1} is the last update of O before this in-place rescale
-          ok = mbar_wait(&o_done[sub], static_cast<uint32_t>((j - 1) & 1), err, abort_flag, DEV_TIMEOUT_SOFTMAX);
+          ok = mbar_wait(o_done, static_cast<uint32_t>((j - 1) & 1), err, abort_flag, DEV_TIMEOUT_SOFTMAX);
           ok = __all_sync(0xffffffffu, ok);
           if (!ok) break;
           tc_fence_after();
@@ -311,11 +372,11 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
 #pragma unroll 1
           for (int h = 0; h < 2; ++h) {
             float t[32];
-            tmem_ld32(t_lane + o_col(sub) + h * 32, t);
+            tmem_ld32(t_lane + O_COL + h * 32, t);
             tmem_ld_wait();
 #pragma unroll
             for (int i = 0; i < 32; ++i) t[i] *= alpha;
-            tmem_st32(t_lane + o_col(sub) + h * 32, t);
+            tmem_st32(t_lane + O_COL + h * 32, t);
           }
           tmem_st_wait();
         }
@@ -323,55 +384,32 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         m_ref = new_ref;
       }
       const float m_use = (m_ref == -INFINITY) ? 0.f : m_ref;
-      // The two softmax warpgroups take turns for the exponentials (they share
-      // the MUFU units of each SM sub-partition): sub-tile 0 goes first, then
-      // each passes the turn on, so one's exp phase overlaps the other's loads,
-      // max and stores.
-      if (n_sub == 2 && (sub == 1 || j > 0)) {
-        ok = mbar_wait(&turn[sub], static_cast<uint32_t>((sub == 0 ? j - 1 : j) & 1), err, abort_flag,
-                       DEV_TIMEOUT_SOFTMAX);
-        ok = __all_sync(0xffffffffu, ok);
-        if (!ok) break;
-      }
-      // p = 2^(s*scale - m) in fp32, row sum in fp32, P packed as fp16 pairs
-      float rs[4] = {0.f, 0.f, 0.f, 0.f};
-      uint32_t pk[64];
+      // p = 2^(s*scale - m) in fp32, row sum in fp32, P packed as fp16 pairs;
+      // stored to TMEM in two 64-key halves
+      float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
 #pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        const float p0 = ex2(fmaf(s[2 * i], sl2, -m_use));
-        const float p1 = ex2(fmaf(s[2 * i + 1], sl2, -m_use));
-        rs[i & 3] += p0 + p1;
-        pk[i] = pack_f16x2(p0, p1);
-      }
-      l += (rs[0] + rs[1]) + (rs[2] + rs[3]);
-      if (n_sub == 2) {
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&turn[sub ^ 1]);
-      }
-      // PV_{j-1} must have read P_{j-1} before P_j replaces it
-      if (j > 0 && !waited) {
-        ok = mbar_wait(&o_done[sub], static_cast<uint32_t>((j - 1) & 1), err, abort_flag, DEV_TIMEOUT_SOFTMAX);
-        ok = __all_sync(0xffffffffu, ok);
-        if (!ok) break;
-        tc_fence_after();
-      }
-      {
-        uint32_t h0[32], h1[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          h0[i] = pk[i];
-          h1[i] = pk[32 + i];
+      for (int h = 0; h < 2; ++h) {
+        uint32_t pk[32];
+        exp_chunk32(s + 64 * h, sl2, m_use, acc0, acc1, pk);
+        exp_chunk32(s + 64 * h + 32, sl2, m_use, acc0, acc1, pk + 16);
+        if (h == 0 && j > 0 && !waited) {
+          // PV_{j-1} must have read P_{j-1} before P_j replaces it
+          ok = mbar_wait(o_done, static_cast<uint32_t>((j - 1) & 1), err, abort_flag, DEV_TIMEOUT_SOFTMAX);
+          ok = __all_sync(0xffffffffu, ok);
+          if (!ok) break;
+          tc_fence_after();
         }
-        tmem_st32u(t_lane + p_col(sub), h0);
-        tmem_st32u(t_lane + p_col(sub) + 32, h1);
+        tmem_st32u(t_lane + P_COL + 32 * h, pk);
       }
+      if (!ok) break;
+      l += (acc0.x + acc0.y) + (acc1.x + acc1.y);
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[sub]);
+      if (lane == 0) mbar_arrive(p_full);
     }
-    if (ok && sub < n_sub && nkv > 0) {
-      ok = mbar_wait(&o_done[sub], static_cast<uint32_t>((nkv - 1) & 1), err, abort_flag, DEV_TIMEOUT_SOFTMAX);
+    if (ok && nkv > 0) {
+      ok = mbar_wait(o_done, static_cast<uint32_t>((nkv - 1) & 1), err, abort_flag, DEV_TIMEOUT_SOFTMAX);
       ok = __all_sync(0xffffffffu, ok);
       if (ok) {
         tc_fence_after();
@@ -379,24 +417,24 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           float t[32];
-          tmem_ld32(t_lane + o_col(sub) + h * 32, t);
+          tmem_ld32(t_lane + O_COL + h * 32, t);
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[h * 32 + i] = t[i];
         }
         tmem_ld_wait();
         const float inv = 1.0f / l;
-        if (r < (sub == 0 ? nq0 : nq1)) {
-          uint4* dst =
-              reinterpret_cast<uint4*>(out + static_cast<size_t>(tile.seq_start + qi) * DIM + head * HDIM);
+        if (r < nq) {
+          bf16* dst = out + static_cast<size_t>(tile.seq_start + qi) * DIM + head * HDIM;
 #pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            uint4 pk4;
-            pk4.x = pack_bf16x2(o[c * 8 + 0] * inv, o[c * 8 + 1] * inv);
-            pk4.y = pack_bf16x2(o[c * 8 + 2] * inv, o[c * 8 + 3] * inv);
-            pk4.z = pack_bf16x2(o[c * 8 + 4] * inv, o[c * 8 + 5] * inv);
-            pk4.w = pack_bf16x2(o[c * 8 + 6] * inv, o[c * 8 + 7] * inv);
-            dst[c] = pk4;
-          }
+          for (int c = 0; c < 4; ++c)
+            st_global_v8(dst + 16 * c, pack_bf16x2(o[16 * c + 0] * inv, o[16 * c + 1] * inv),
+                         pack_bf16x2(o[16 * c + 2] * inv, o[16 * c + 3] * inv),
+                         pack_bf16x2(o[16 * c + 4] * inv, o[16 * c + 5] * inv),
+                         pack_bf16x2(o[16 * c + 6] * inv, o[16 * c + 7] * inv),
+                         pack_bf16x2(o[16 * c + 8] * inv, o[16 * c + 9] * inv),
+                         pack_bf16x2(o[16 * c + 10] * inv, o[16 * c + 11] * inv),
+                         pack_bf16x2(o[16 * c + 12] * inv, o[16 * c + 13] * inv),
+                         pack_bf16x2(o[16 * c + 14] * inv, o[16 * c + 15] * inv));
         }
       }
     }
@@ -412,18 +450,30 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
 
 }  // namespace
 
-void attention(const CUtensorMap& Q, const CUtensorMap& K, const CUtensorMap& V, const AttnTile* tiles,
-               int n_tiles, int chunk, bf16* out, int* err, cudaStream_t s) {
-  if (n_tiles <= 0) return;
-  static bool attr_done[64] = {false};
+bool attention_ready() {
+  static int checked[64] = {0};  // 0 unchecked, 1 ok, -1 unusable
   int dev = 0;
-  cudaGetDevice(&dev);
-  if (!attr_done[dev & 63]) {
-    cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, ATT_SMEM);
-    attr_done[dev & 63] = true;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  int& state = checked[dev & 63];
+  if (state == 0) {
+    // setmaxnreg.inc waits for registers the block was launched with: refuse
+    // to launch unless the launch register count covers the split
+    cudaFuncAttributes fa;
+    state = (cudaFuncGetAttributes(&fa, k_attention) == cudaSuccess && fa.numRegs >= ATT_LAUNCH_REGS &&
+             cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, ATT_SMEM) ==
+                 cudaSuccess)
+                ? 1
+                : -1;
   }
-  dim3 grid(n_tiles, HEADS);
-  k_attention<<<grid, ATT_THREADS, ATT_SMEM, s>>>(Q, K, V, tiles, chunk, out, err);
+  return state > 0;
+}
+
+bool attention(const CUtensorMap& Q, const CUtensorMap& K, const CUtensorMap& V, const AttnTile* tiles,
+               int n_tiles, int chunk, bf16* out, int* err, cudaStream_t s) {
+  if (n_tiles <= 0) return true;
+  if (!attention_ready() || n_tiles > ATT_MAX_TILES) return false;
+  k_attention<<<dim3(HEADS, n_tiles), ATT_THREADS, ATT_SMEM, s>>>(Q, K, V, tiles, chunk, out, err);
+  return true;
 }
 
 }  // namespace lx

@@ -69,6 +69,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait that may suspend the thread for up to `hint_ns` (it resumes as soon
+// as the phase completes), so a waiting thread does not take issue slots from
+// the working warps of its SM sub-partition.
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+constexpr uint32_t LX_WAIT_SUSPEND_NS = 1000000u;  // 1 ms per suspended try
+
 // Bounded wait for the phase of the given parity to complete.  Returns false
 // (after recording `code` in *err and raising *abort) when the wait exceeds
 // the timeout, or when another role of the CTA has already aborted.
@@ -76,15 +93,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
                                           int code) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
-  for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 63u) == 0) {
-      if (*abort_flag) return false;
-      if (global_timer_ns() - t0 > LX_WAIT_TIMEOUT_NS) {
-        if (err) atomicCAS(err, 0, code);
-        *abort_flag = 1;
-        return false;
-      }
+  for (;;) {
+    if (mbar_try_wait_hint(bar, parity, LX_WAIT_SUSPEND_NS)) return true;
+    if (*abort_flag) return false;
+    if (global_timer_ns() - t0 > LX_WAIT_TIMEOUT_NS) {
+      if (err) atomicCAS(err, 0, code);
+      *abort_flag = 1;
+      return false;
     }
   }
 }

@@ -10,6 +10,7 @@
 //   final AdaLN-mod -> proj_out GEMM (N=80) -> CFG Euler update
 // The reference runs the same steps as one GGML graph per Euler step with the
 // Euler/CFG update on the host (src/flow/flow.cpp:240-274).
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -446,12 +447,18 @@ Plan make_plan(int n_utt, const int32_t* lengths, bool cfg_pairs, int chunk, int
   for (int s = 0; s < p.n_seq; ++s)
     for (int q0 = 0; q0 < p.seq_len[s]; q0 += ATT_Q_ROWS)
       p.tiles.push_back(AttnTile{p.seq_start[s], p.seq_len[s], q0, 0});
+  // longest query blocks first: the shortest CTAs fill the last wave
+  std::stable_sort(p.tiles.begin(), p.tiles.end(), [chunk](const AttnTile& a, const AttnTile& b) {
+    return attn_tile_keys(a, chunk) > attn_tile_keys(b, chunk);
+  });
   p.key = plan_key(n_utt, lengths, cfg_pairs, chunk, steps);
   return p;
 }
 
 int ensure_workspace(lx_flow* h, const Plan& p, size_t in_floats, int n_utt) {
   Workspace& w = h->ws;
+  if (p.tiles.size() > static_cast<size_t>(ATT_MAX_TILES))
+    return h->fail(LX_ERR_SHAPE, "batch too large: more than 65535 attention query blocks");
   const bool grow = p.R > w.capR || p.Rs > w.capRs || p.F > w.capF ||
                     static_cast<int>(p.tiles.size()) > w.capTiles || in_floats > w.capIn ||
                     static_cast<size_t>(n_utt) > w.capUtt;
@@ -770,6 +777,7 @@ int lx_flow_create(int device, lx_flow** out) {
   cudaDeviceProp prop;
   if (cudaGetDeviceProperties(&prop, device) != cudaSuccess || prop.major != 10) return LX_ERR_CUDA;
   if (cudaSetDevice(device) != cudaSuccess) return LX_ERR_CUDA;
+  if (!attention_ready()) return LX_ERR_CUDA;
   std::unique_ptr<lx_flow> h(new lx_flow());
   h->device = device;
   if (cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking) != cudaSuccess) return LX_ERR_CUDA;

@@ -61,14 +61,14 @@ __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}\n"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
       : "memory");
   return ok != 0;
 }
@@ -76,17 +76,15 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t pa
 // Bounded wait (acquire at cluster scope: the barrier receives remote arrivals).
 __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int* err, volatile int* abort_flag,
                                                   int code) {
-  if (mbar_try_wait_cluster(bar, parity)) return true;
+  if (mbar_try_wait_cluster(bar, parity, 0u)) return true;
   const uint64_t t0 = global_timer_ns();
-  for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait_cluster(bar, parity)) return true;
-    if ((i & 63u) == 0) {
-      if (*abort_flag) return false;
-      if (global_timer_ns() - t0 > LX_WAIT_TIMEOUT_NS) {
-        if (err) atomicCAS(err, 0, code);
-        *abort_flag = 1;
-        return false;
-      }
+  for (;;) {
+    if (mbar_try_wait_cluster(bar, parity, LX_WAIT_SUSPEND_NS)) return true;
+    if (*abort_flag) return false;
+    if (global_timer_ns() - t0 > LX_WAIT_TIMEOUT_NS) {
+      if (err) atomicCAS(err, 0, code);
+      *abort_flag = 1;
+      return false;
     }
   }
 }

@@ -37,8 +37,8 @@ bool tmap_bf16(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, u
 bool tmap_f32(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows,
               uint32_t box_cols);
 
-// Query rows per attention CTA (two 128-row sub-tiles).
-constexpr int ATT_Q_ROWS = 256;
+// Query rows per attention CTA.
+constexpr int ATT_Q_ROWS = 128;
 
 struct AttnTile {
   int seq_start;  // first packed row of the sequence
@@ -46,6 +46,15 @@ struct AttnTile {
   int q0;         // first query of this block (multiple of ATT_Q_ROWS), relative to seq_start
   int pad;
 };
+
+// Keys visible to the last query of tile t (the keys the attention CTA of t
+// walks): the sequence length, or the end of that query's chunk.
+inline int attn_tile_keys(const AttnTile& t, int chunk) {
+  const int nq = t.seq_len - t.q0 < ATT_Q_ROWS ? t.seq_len - t.q0 : ATT_Q_ROWS;
+  if (chunk <= 0) return t.seq_len;
+  const int end = ((t.q0 + nq - 1) / chunk + 1) * chunk;
+  return end < t.seq_len ? end : t.seq_len;
+}
 
 // ---- GEMMs (tcgen05) --------------------------------------------------------
 // `bn` is the N tile (128 or 256; pick_bn chooses by wave count); the B tensor
@@ -97,7 +106,14 @@ void conv_pos(const CUtensorMap& A, const CUtensorMap& B, int Ms, const float* b
 // out[row, 64h..64h+63] for every valid query row of every tile; chunk > 0
 // applies the block-causal chunk mask, keys >= seq_len are always masked.
 // Q, K: bf16 [R][1024] maps, V: fp16 [R][1024] map; all boxes 128 rows x 64.
-void attention(const CUtensorMap& Q, const CUtensorMap& K, const CUtensorMap& V, const AttnTile* tiles,
+// Tiles in any order (longest first balances the last wave).  Returns false,
+// launching nothing, when the kernel cannot be launched safely (see
+// attention_ready) or n_tiles > ATT_MAX_TILES.
+constexpr int ATT_MAX_TILES = 65535;
+// True when the attention kernel's launch register count covers its
+// setmaxnreg split on the current device (checked once per device).
+bool attention_ready();
+bool attention(const CUtensorMap& Q, const CUtensorMap& K, const CUtensorMap& V, const AttnTile* tiles,
                int n_tiles, int chunk, bf16* out, int* err, cudaStream_t s);
 
 // ---- element-wise / row kernels -----------------------------------------

@@ -93,8 +93,10 @@ int lx_flow_op_attention(int n_seq, const int32_t* lengths, const void* q, const
         !tmap_bf16(&tv, vh, R, DIM, DIM, 128, 64)) {
       rc = LX_ERR_ARG;
     } else {
-      attention(tq, tk, tv, d_tiles, static_cast<int>(tiles.size()), chunk, static_cast<bf16*>(out), d_err, s);
-      rc = sync_check(s, d_err);
+      if (!attention(tq, tk, tv, d_tiles, static_cast<int>(tiles.size()), chunk, static_cast<bf16*>(out), d_err, s))
+        rc = LX_ERR_CUDA;
+      else
+        rc = sync_check(s, d_err);
     }
   }
   if (vh) cudaFree(vh);

@@ -13,7 +13,7 @@
 //
 // Limit (checked on the host; a larger call returns LX_ERR_ARG before any
 // device work is queued): packed rows R = sum_i round_up(len_i, 8) <=
-// LX_STATIC_ATT_MAX_ROWS (4096).  Query tiles = sum_i ceil(len_i / 256) <= R / 8,
+// LX_STATIC_ATT_MAX_ROWS (4096).  Query tiles = sum_i ceil(len_i / 128) <= R / 8,
 // so 512 tile slots always suffice.  The static storage is 8 MiB of fp16 V
 // ([4096][1024]) + 8 KiB of tiles + one error word per device.
 //
@@ -119,7 +119,7 @@ extern "C" int lx_flow_op_attention_static(int n_seq, const int32_t* lengths, co
     return LX_ERR_CUDA;
   const int n8 = rows * (DIM / 8);
   k_v_to_f16_static<<<(n8 + 255) / 256, 256, 0, s>>>(static_cast<const bf16*>(v), sc.v, n8);
-  attention(tq, tk, tv, sc.tiles, n_tiles, chunk, static_cast<bf16*>(out), sc.err, s);
+  if (!attention(tq, tk, tv, sc.tiles, n_tiles, chunk, static_cast<bf16*>(out), sc.err, s)) return LX_ERR_CUDA;
   if (cudaGetLastError() != cudaSuccess || cudaStreamSynchronize(s) != cudaSuccess) return LX_ERR_CUDA;
   int e = 0;
   if (cudaMemcpy(&e, sc.err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return LX_ERR_CUDA;
