@@ -211,6 +211,94 @@ def run_reference(args):
 
 
 # ---------------------------------------------------------------------------
+# BASELINE config 1 (fused-op microbench) and config 4 (streaming chunks)
+# ---------------------------------------------------------------------------
+CFG1_OPS = (("adaln", 0), ("gate_residual", 1), ("rotary", 2), ("gelu_tanh", 3))
+
+
+def bench_cfg1(dev, stream, rows=2000, sets=16, reps=20):
+    """Standalone fused ops on [2000, 1024] (seed 1, mods N(0, 0.5)), fp32 in
+    and bf16 in, fp32 out; `sets` rotating buffer sets (> L2) so every launch
+    reads HBM.  GB/s = algorithmic bytes / device time per launch."""
+    import torch
+    from larynx_b200 import flow
+    g = torch.Generator(device="cpu").manual_seed(1)
+    D = 1024
+    mods = (torch.randn(2, 6 * D, generator=g) * 0.5).to(dev)
+    shift, scale, gate = mods[0, :D].contiguous(), mods[0, D:2 * D].contiguous(), mods[1, :D].contiguous()
+    pos = (torch.arange(rows, dtype=torch.int32) % 1500).to(dev)
+    peak = load_peaks()["hbm"]
+    out = {}
+    res = [torch.randn(rows, D, generator=g).to(dev) for _ in range(sets)]  # fp32 residual (gate_residual)
+    ys = [torch.empty(rows, D, device=dev) for _ in range(sets)]            # fp32 outputs
+    for bf in (False, True):
+        xs = [torch.randn(rows, D, generator=g).to(dev) for _ in range(sets)]
+        if bf:
+            xs = [x.to(torch.bfloat16) for x in xs]
+        sin = 2 if bf else 4
+        for name, op in CFG1_OPS:
+            if op == 1:  # x_res += gate * branch: residual read + write, branch read
+                nbytes = rows * D * (8 + sin)
+                launch = lambda i: flow.op(1, bf, rows, res[i % sets].data_ptr(), xs[i % sets].data_ptr(),
+                                           gate_ptr=gate.data_ptr(), stream=stream.cuda_stream)
+            else:
+                nbytes = rows * D * (sin + 4)
+                launch = lambda i, op=op: flow.op(op, bf, rows, xs[i % sets].data_ptr(), ys[i % sets].data_ptr(),
+                                                  shift_ptr=shift.data_ptr(), scale_ptr=scale.data_ptr(),
+                                                  pos_ptr=pos.data_ptr(), stream=stream.cuda_stream)
+            with torch.cuda.stream(stream):
+                for i in range(sets):
+                    launch(i)
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                for i in range(sets * reps):
+                    launch(i)
+                e1.record(stream)
+                stream.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / (sets * reps)
+            gbs = nbytes / (us * 1e-6) / 1e9
+            out[f"{name}_{'bf16' if bf else 'f32'}_in"] = {"us": round(us, 2), "GB/s": round(gbs, 1),
+                                                             "frac_of_hbm": round(gbs / peak, 3)}
+    out["_about"] = (f"[{rows},1024] per launch, {sets} rotating buffer sets (> L2), fp32 out; gate_residual "
+                     "updates an fp32 residual with an fp32/bf16 branch; frac of the measured HBM copy bandwidth")
+    return out
+
+
+def bench_cfg4(dec, dev, stream, streams=256, iters=3):
+    """256 streams, each one 50-frame chunk + 6-frame lookahead after
+    ctx ~ 50 * U{0..10} frames of context (seed 4), block-causal chunk mask
+    (chunk 50), 10-step CFG decode of every stream's whole sequence (stateless
+    recompute).  Counts the 50 emitted frames per stream."""
+    import torch
+    out = {}
+    rng = np.random.default_rng(4)
+    cases = {"mixed_ctx": (50 * rng.integers(0, 11, streams) + 56).astype(np.int32),
+             "worst_ctx500": np.full(streams, 556, np.int32)}
+    for name, L in cases.items():
+        mu, cond, spks, noise = cfg3_inputs(L, seed=4)
+        t = [torch.from_numpy(a).to(dev) for a in (mu, cond, spks, noise)]
+        o = torch.empty_like(t[0])
+        times = []
+        with torch.cuda.stream(stream):
+            for i in range(iters + 2):
+                a0 = torch.cuda.Event(enable_timing=True)
+                a1 = torch.cuda.Event(enable_timing=True)
+                a0.record(stream)
+                dec.decode_device(L, t[0].data_ptr(), t[1].data_ptr(), t[2].data_ptr(), t[3].data_ptr(),
+                                  o.data_ptr(), chunk=50, stream=stream.cuda_stream)
+                a1.record(stream)
+                stream.synchronize()
+                if i >= 2:
+                    times.append(a0.elapsed_time(a1))
+        ms = float(np.median(times))
+        out[name] = {"ms_per_chunk_step": round(ms, 3), "emitted_frames_per_s": round(streams * 50 / (ms * 1e-3), 1),
+                     "frames_decoded_per_s": round(float(L.sum()) / (ms * 1e-3), 1),
+                     "frames_per_batch": int(L.sum())}
+    return out
+
+
+# ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
 def run_ours(args):
@@ -222,6 +310,11 @@ def run_ours(args):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dist_on = world > 1
+    # stdout carries exactly one JSON line: anything a library prints there
+    # (e.g. NCCL's version banner) is sent to stderr instead
+    sys.stdout.flush()
+    json_fd = os.dup(1)
+    os.dup2(2, 1)
     if dist_on:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
@@ -384,6 +477,35 @@ def run_ours(args):
         extra["cfg2_T1000_latency_ms"] = float(np.median(times))
         extra["cfg2_frames_per_s"] = 1000.0 / (float(np.median(times)) * 1e-3)
 
+    if dist_on:
+        # strong-scaling view of config 3: the one 64-utterance set split across
+        # the ranks by LPT over the decode cost (larynx_b200.shard)
+        from larynx_b200 import shard
+        mine = shard.lpt_partition(lengths, world)[rank]
+        Ls = lengths[mine]
+        ms_, cs_, ss_, ns_ = cfg3_inputs(Ls, seed=3000)
+        ts_ = [torch.from_numpy(a).to(dev) for a in (ms_, cs_, ss_, ns_)]
+        os_ = torch.empty_like(ts_[0])
+        with torch.cuda.stream(stream):
+            for i in range(3):
+                if i == 2:
+                    barrier()
+                    b0 = torch.cuda.Event(enable_timing=True)
+                    b1 = torch.cuda.Event(enable_timing=True)
+                    b0.record(stream)
+                dec.decode_device(Ls, ts_[0].data_ptr(), ts_[1].data_ptr(), ts_[2].data_ptr(), ts_[3].data_ptr(),
+                                  os_.data_ptr(), stream=stream.cuda_stream)
+            b1.record(stream)
+            stream.synchronize()
+        sms = max_over_ranks(b0.elapsed_time(b1))
+        extra["cfg3_lpt_strong"] = {"value": float(lengths.sum()) / (sms * 1e-3), "unit": UNIT,
+                                    "ms": sms, "utterances_this_rank": int(len(mine)),
+                                    "about": "the 64-utterance set LPT-sharded across ranks (strong scaling)"}
+    if not args.no_cfg1:
+        extra["cfg1_ops"] = bench_cfg1(dev, stream)
+    if not args.no_cfg4:
+        extra["cfg4_stream"] = bench_cfg4(dec, dev, stream)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         from oracle import flow_oracle as fo
@@ -403,7 +525,8 @@ def run_ours(args):
                 "config": config_block(world, lengths), "rtf": (ms / args.steps * 1e-3) / (tot / 50.0),
                 "e2e": e2e, "gpu_launches": int(launches), "roofline": roofline, "cpu_baseline": cpu,
                 "clocks": clk, "kernels": breakdown, "attention": attn, "finite": finite, **extra}
-        print(json.dumps(line), flush=True)
+        sys.stdout.flush()
+        os.write(json_fd, (json.dumps(line) + "\n").encode())
     dec.close()
     if dist_on:
         dist.barrier()
@@ -420,6 +543,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-cfg2", action="store_true")
+    ap.add_argument("--no-cfg1", action="store_true")
+    ap.add_argument("--no-cfg4", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

@@ -26,8 +26,7 @@
 //               half (w - 4) / 4 (two warps per SM sub-partition hide each
 //               other's TMEM / global latencies); each warp arrives on the
 //               leader's `tempty` barrier (8 local + 8 remote arrivals)
-// No TMA load in this file multicasts; every copy lands in the issuing CTA's
-// own shared memory.
+// Every TMA copy in this file lands in the issuing CTA's own shared memory.
 #pragma once
 
 #include "common.cuh"

@@ -1,0 +1,81 @@
+"""Multi-GPU host logic on the CPU: the LPT shard partition and the rank-0
+gather, the latter with two gloo ranks (no GPU)."""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+
+from larynx_b200 import shard
+
+
+def _cfg3(n=64):
+    return np.random.default_rng(3).integers(100, 1501, n).astype(np.int32)
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_lpt_partition_covers_and_balances(world):
+    L = _cfg3()
+    parts = shard.lpt_partition(L, world)
+    allidx = np.concatenate(parts)
+    assert sorted(allidx.tolist()) == list(range(len(L)))
+    loads = shard.shard_loads(L, parts)
+    cost = shard.utterance_cost(L)
+    lower = max(cost.sum() / world, cost.max())
+    # Graham's bound for LPT: at most 4/3 - 1/(3m) of the optimum
+    assert loads.max() <= (4 / 3 - 1 / (3 * world)) * lower + 1e-6
+    # and in practice within a few percent of the mean on this workload
+    assert loads.max() / (cost.sum() / world) < 1.06
+
+
+def test_cost_is_quadratic_in_length():
+    c = shard.utterance_cost([1000, 2000])
+    assert c[1] > 2 * c[0]  # attention's T^2 term
+
+
+def test_lpt_errors():
+    with pytest.raises(ValueError):
+        shard.lpt_partition([100], 0)
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, lengths, q):
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        parts = shard.lpt_partition(lengths, world)
+        mine = parts[rank]
+        # stand-in for each utterance's decoded mel: [80, T] filled with its index
+        results = [np.full((80, int(lengths[i])), float(i), np.float32) for i in mine]
+        out = shard.gather_to_rank0(results, mine, len(lengths))
+        if rank == 0:
+            ok = all(o.shape == (80, int(lengths[i])) and float(o[0, 0]) == float(i) for i, o in enumerate(out))
+            q.put(ok)
+        else:
+            q.put(out is None)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gather_two_gloo_ranks():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    L = _cfg3(17)
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, L, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+        assert p.exitcode == 0
+    res = [q.get(timeout=10) for _ in range(2)]
+    assert all(res)
