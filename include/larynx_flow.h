@@ -98,6 +98,22 @@ int lx_flow_infer(lx_flow* h, const int32_t* prompt_tokens, int n_prompt, const 
                   const float* prompt_feat, int mel_len1, const float* spk_embedding, const float* noise_z,
                   float* mel_out, size_t mel_cap, lx_flow_debug* debug);
 
+/* lx_flow_infer with the reference's `finalize` flag (flow_reference.py:531-563,
+ * CosyVoice3 CausalMaskedDiffWithXvec.inference; the reference's C++ path
+ * implements only finalize=True, src/flow/flow.cpp:110 / docs/FLOW.md §5).
+ * finalize != 0 is lx_flow_infer.  finalize == 0 is the streaming call: the
+ * last 3 tokens are PreLookahead look-ahead context (they replace its zero
+ * padding and produce no frames), so MEL_T = 2 * (n_prompt + n_tokens - 3)
+ * and mel_out receives [80][MEL_T - mel_len1].  The CFM noise is the first
+ * MEL_T columns of noise_z (a [80][MEL_T] array) or of the noise bank.
+ * chunk > 0 applies the block-causal chunk mask (as lx_flow_batch.chunk; the
+ * streaming attention of upstream CosyVoice3 with static_chunk_size frames);
+ * chunk == 0 is the reference's full attention.  Stage captures (debug) are
+ * taken with full attention. */
+int lx_flow_infer_ex(lx_flow* h, const int32_t* prompt_tokens, int n_prompt, const int32_t* tokens, int n_tokens,
+                     const float* prompt_feat, int mel_len1, const float* spk_embedding, const float* noise_z,
+                     int finalize, int chunk, float* mel_out, size_t mel_cap, lx_flow_debug* debug);
+
 /* Batched decode at the estimator/CFM level (the north-star hot path;
  * extends FlowDecoder::infer's Euler loop, src/flow/flow.cpp:202-274, to many
  * utterances): each utterance u of T_u frames is decoded with its own

@@ -1,25 +1,28 @@
 // Fused flash attention for the DiT blocks on sm_100a (tcgen05 + TMEM).
 //
-// One CTA = one (128-query block, head) of one sequence, head_dim = 64; two
-// CTAs share each SM (256 threads, 128 registers per thread at launch,
-// 80 KB of shared memory and 256 tensor-memory columns each).  Two resident
-// CTAs are what keeps the MUFU units busy: while one CTA loads its scores,
-// reduces the row max, stores P or runs its prologue / epilogue, the other
-// one's exponentials run, with no hand-off between them.
+// Persistent: two CTAs per SM (256 threads, 128 registers per thread at
+// launch, 99 KB of shared memory and 256 tensor-memory columns each) walk the
+// work items (128-query block, head), head_dim = 64; the host orders the
+// blocks longest first and CTA c takes items c, c + grid, ...  Two resident
+// CTAs keep the MUFU units busy: while one loads its scores, reduces the row
+// max or stores P, the other one's exponentials run.  Within a CTA the next
+// item's Q (double-buffered) and first QK^T run under the current item's last
+// softmax step, so there is no per-item prologue or launch gap.
 //
 // Tensor memory (256 columns): S [0,128), P [128,192) (fp16 pairs), O [192,256).
-//   warp 0      TMA: the Q tile once, then the K tiles [128 keys x 64] (bf16)
-//               through a 2-slot ring released as soon as QK^T has read them
+//   warp 0      TMA: each item's Q tile (2 slots), then its K tiles [128 keys x
+//               64] (bf16) through a 2-slot ring released as soon as QK^T has
+//               read them
 //   warp 2      TMA: the V tiles [128 keys x 64] (fp16, row-major as the QKV
 //               GEMM wrote it; the PV MMA reads it as an MN-major operand, so
 //               no transpose exists anywhere) through a 2-slot ring released
 //               after PV.  Separate rings keep the K load of tile j+1 off the
 //               softmax -> PV -> release chain of tile j-1.
-//   warp 1      lane 0 issues the MMAs: S = Q K_j+1^T (M=128, N=128, K=64,
-//               bf16) as soon as the softmax has pulled S_j into registers,
-//               so QK^T of tile j+1 runs under the softmax of tile j; then
-//               O += P_j V_j (M=128, N=64, K=128, fp16, P read from tensor
-//               memory)
+//   warp 1      lane 0 issues the MMAs: S = Q K^T (M=128, N=128, K=64, bf16)
+//               one key tile ahead of the softmax (across item boundaries),
+//               then O += P V (M=128, N=64, K=128, fp16, P read from tensor
+//               memory; an item's first PV waits until the softmax has read
+//               the previous item's O)
 //   warp 3      idle (warpgroup 0 lowers its registers with setmaxnreg)
 //   warps 4..7  softmax: thread = query row; S row from TMEM into registers,
 //               key-padding / block-causal mask on boundary tiles only,
@@ -28,8 +31,7 @@
 //               shared memory, whose bandwidth the MMA operands need).  O is
 //               rescaled in place only when a row's running max grows by more
 //               than 2^8 (the reference max is otherwise kept, which is exact).
-// The host orders the query blocks longest first, so the shortest CTAs fill
-// the last wave.  No score matrix ever reaches HBM.
+// No score matrix ever reaches HBM.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -50,7 +52,7 @@ constexpr int ATT_STAGES = 2;
 constexpr int Q_BYTES = 128 * 64 * 2;  // 16 KB
 constexpr int K_BYTES = 128 * 64 * 2;  // 16 KB
 constexpr int V_BYTES = 128 * 64 * 2;  // 16 KB: 128 keys x 64 fp16 values (MN-major B of PV)
-constexpr int ATT_SMEM = 1024 + Q_BYTES + ATT_STAGES * (K_BYTES + V_BYTES) + 256;
+constexpr int ATT_SMEM = 1024 + 2 * Q_BYTES + ATT_STAGES * (K_BYTES + V_BYTES) + 256;
 constexpr uint32_t ATT_TMEM_COLS = 256;
 constexpr uint32_t S_COL = 0, P_COL = 128, O_COL = 192;
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units: P <= 2^8
@@ -169,18 +171,38 @@ __device__ __forceinline__ void exp_chunk32(const float* s, float sl2, float m, 
   }
 }
 
+// One work item = (query block, head); items are numbered block-major (the
+// host sorts blocks longest first) and CTA c takes items c, c + grid, ...
+struct AttnItem {
+  AttnTile t;
+  int head, nq, nkv;
+};
+
+__device__ __forceinline__ AttnItem load_item(const AttnTile* __restrict__ tiles, int idx, int chunk) {
+  AttnItem it;
+  it.t = tiles[idx / HEADS];
+  it.head = idx % HEADS;
+  it.nq = min(128, it.t.seq_len - it.t.q0);
+  // keys visible to the last query of the block
+  int kv_end = it.t.seq_len;
+  if (chunk > 0) kv_end = min(it.t.seq_len, ((it.t.q0 + it.nq - 1) / chunk + 1) * chunk);
+  it.nkv = (kv_end + 127) / 128;
+  return it;
+}
+
 __global__ void __launch_bounds__(ATT_THREADS, 2)
     k_attention(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                const __grid_constant__ CUtensorMap tmV, const AttnTile* __restrict__ tiles, int chunk,
+                const __grid_constant__ CUtensorMap tmV, const AttnTile* __restrict__ tiles, int n_items, int chunk,
                 bf16* __restrict__ out, int* err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sK = sQ + Q_BYTES;
+  uint8_t* sQ = smem;  // 2 slots: the next item's Q loads under the current item
+  uint8_t* sK = sQ + 2 * Q_BYTES;
   uint8_t* sV = sK + ATT_STAGES * K_BYTES;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sV + ATT_STAGES * V_BYTES);
-  uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;
+  uint64_t* q_full = bars;       // [2]
+  uint64_t* q_empty = bars + 2;  // [2]
+  uint64_t* k_full = bars + 4;
   uint64_t* k_empty = k_full + ATT_STAGES;
   uint64_t* v_full = k_empty + ATT_STAGES;
   uint64_t* v_empty = v_full + ATT_STAGES;
@@ -188,22 +210,19 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
   uint64_t* s_empty = s_full + 1;
   uint64_t* p_full = s_empty + 1;
   uint64_t* o_done = p_full + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 1);
+  uint64_t* o_free = o_done + 1;  // the softmax has read the finished O of an item
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_free + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int head = blockIdx.x;
-  const AttnTile tile = tiles[blockIdx.y];
-  const int len = tile.seq_len;
-  const int nq = min(128, len - tile.q0);
-  // keys visible to the last query of the block
-  int kv_end = len;
-  if (chunk > 0) kv_end = min(len, ((tile.q0 + nq - 1) / chunk + 1) * chunk);
-  const int nkv = (kv_end + 127) / 128;
+  const int grid = gridDim.x;
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+    }
     for (int s = 0; s < ATT_STAGES; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
@@ -214,6 +233,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
     mbar_init(s_empty, 4);
     mbar_init(p_full, 4);
     mbar_init(o_done, 1);
+    mbar_init(o_free, 4);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -230,212 +250,228 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
     regs_dec<REGS_PRODUCER>();
     if (warp == 0) {
       if (lane == 0) {
+        // Q of every item, then its K tiles (global step g: ring slot g % 2)
         tma_prefetch_desc(&tmQ);
         tma_prefetch_desc(&tmK);
         tma_prefetch_desc(&tmV);
-        mbar_arrive_expect_tx(q_full, Q_BYTES);
-        tma_load_2d(sQ, &tmQ, q_full, head * HDIM, tile.seq_start + tile.q0);
-        int stage = 0;
-        uint32_t phase = 0;
-        for (int j = 0; j < nkv; ++j) {
-          if (!mbar_wait(&k_empty[stage], phase ^ 1u, err, abort_flag, DEV_TIMEOUT_PRODUCER)) break;
-          mbar_arrive_expect_tx(&k_full[stage], K_BYTES);
-          tma_load_2d(sK + stage * K_BYTES, &tmK, &k_full[stage], head * HDIM, tile.seq_start + j * 128);
-          if (++stage == ATT_STAGES) {
-            stage = 0;
-            phase ^= 1u;
+        bool ok = true;
+        int g = 0, n = 0;
+        for (int idx = blockIdx.x; ok && idx < n_items; idx += grid, ++n) {
+          const AttnItem it = load_item(tiles, idx, chunk);
+          const int qs = n & 1;
+          if (!(ok = mbar_wait(&q_empty[qs], ((n >> 1) & 1) ^ 1u, err, abort_flag, DEV_TIMEOUT_PRODUCER))) break;
+          mbar_arrive_expect_tx(&q_full[qs], Q_BYTES);
+          tma_load_2d(sQ + qs * Q_BYTES, &tmQ, &q_full[qs], it.head * HDIM, it.t.seq_start + it.t.q0);
+          for (int j = 0; j < it.nkv; ++j, ++g) {
+            const int st = g & 1;
+            if (!(ok = mbar_wait(&k_empty[st], ((g >> 1) & 1) ^ 1u, err, abort_flag, DEV_TIMEOUT_PRODUCER))) break;
+            mbar_arrive_expect_tx(&k_full[st], K_BYTES);
+            tma_load_2d(sK + st * K_BYTES, &tmK, &k_full[st], it.head * HDIM, it.t.seq_start + j * 128);
           }
         }
       }
     } else if (warp == 2) {
       if (lane == 0) {
-        int stage = 0;
-        uint32_t phase = 0;
-        for (int j = 0; j < nkv; ++j) {
-          if (!mbar_wait(&v_empty[stage], phase ^ 1u, err, abort_flag, DEV_TIMEOUT_PRODUCER)) break;
-          mbar_arrive_expect_tx(&v_full[stage], V_BYTES);
-          tma_load_2d(sV + stage * V_BYTES, &tmV, &v_full[stage], head * HDIM, tile.seq_start + j * 128);
-          if (++stage == ATT_STAGES) {
-            stage = 0;
-            phase ^= 1u;
+        bool ok = true;
+        int g = 0;
+        for (int idx = blockIdx.x; ok && idx < n_items; idx += grid) {
+          const AttnItem it = load_item(tiles, idx, chunk);
+          for (int j = 0; j < it.nkv; ++j, ++g) {
+            const int st = g & 1;
+            if (!(ok = mbar_wait(&v_empty[st], ((g >> 1) & 1) ^ 1u, err, abort_flag, DEV_TIMEOUT_PRODUCER))) break;
+            mbar_arrive_expect_tx(&v_full[st], V_BYTES);
+            tma_load_2d(sV + st * V_BYTES, &tmV, &v_full[st], it.head * HDIM, it.t.seq_start + j * 128);
           }
         }
       }
     } else if (warp == 1) {
       if (lane == 0) {
-        const uint64_t dq = sdesc_sw128(smem_u32(sQ));
+        // Global step g runs S_g = Q K_g^T, then PV_{g-1}: the QK^T of the next
+        // key tile (or of the next item's first tile) is always in flight
+        // while the softmax works on the current one.
+        const uint64_t dq0 = sdesc_sw128(smem_u32(sQ));
         const uint64_t dk0 = sdesc_sw128(smem_u32(sK));
         const uint64_t dv0 = sdesc_sw128_mn(smem_u32(sV));
         const uint32_t s_t = tmem_base + S_COL;
         const uint32_t p_t = tmem_base + P_COL;
         const uint32_t o_t = tmem_base + O_COL;
-        bool ok = mbar_wait(q_full, 0, err, abort_flag, DEV_TIMEOUT_MMA);
-        if (ok) ok = mbar_wait(&k_full[0], 0, err, abort_flag, DEV_TIMEOUT_MMA);
-        if (ok) {
+        bool ok = true;
+        int g = 0, n = 0, prev_j = 0, prev_n = 0;
+        // PV of global step gp (key tile jp of the CTA's item np)
+        auto issue_pv_step = [&](int gp, int jp, int np) -> bool {
+          bool w = mbar_wait(p_full, static_cast<uint32_t>(gp & 1), err, abort_flag, DEV_TIMEOUT_MMA);
+          if (w) w = mbar_wait(&v_full[gp & 1], static_cast<uint32_t>((gp >> 1) & 1), err, abort_flag, DEV_TIMEOUT_MMA);
+          // the first PV of an item overwrites O: the previous item's O must have been read
+          if (w && jp == 0 && np > 0)
+            w = mbar_wait(o_free, static_cast<uint32_t>((np - 1) & 1), err, abort_flag, DEV_TIMEOUT_MMA);
+          if (!w) return false;
           tc_fence_after();
-          issue_s(s_t, dq, dk0);
-          umma_commit(s_full);
-          umma_commit(&k_empty[0]);
-        }
-        int stage = 0;
-        uint32_t phase = 0;
-        for (int j = 0; ok && j < nkv; ++j) {
-          int st_n = stage + 1;
-          uint32_t ph_n = phase;
-          if (st_n == ATT_STAGES) {
-            st_n = 0;
-            ph_n ^= 1u;
-          }
-          if (j + 1 < nkv) {
-            ok = mbar_wait(&k_full[st_n], ph_n, err, abort_flag, DEV_TIMEOUT_MMA);
-            if (ok) ok = mbar_wait(s_empty, static_cast<uint32_t>(j & 1), err, abort_flag, DEV_TIMEOUT_MMA);
+          issue_pv(o_t, p_t, dv0 + static_cast<uint64_t>(((gp & 1) * V_BYTES) >> 4), jp > 0);
+          umma_commit(o_done);
+          umma_commit(&v_empty[gp & 1]);
+          return true;
+        };
+        for (int idx = blockIdx.x; ok && idx < n_items; idx += grid, ++n) {
+          const AttnItem it = load_item(tiles, idx, chunk);
+          const int qs = n & 1;
+          const uint64_t dq = dq0 + static_cast<uint64_t>((qs * Q_BYTES) >> 4);
+          if (!(ok = mbar_wait(&q_full[qs], static_cast<uint32_t>((n >> 1) & 1), err, abort_flag, DEV_TIMEOUT_MMA)))
+            break;
+          for (int j = 0; j < it.nkv; ++j, ++g) {
+            ok = mbar_wait(&k_full[g & 1], static_cast<uint32_t>((g >> 1) & 1), err, abort_flag, DEV_TIMEOUT_MMA);
+            // S_{g-1} must have been read by the softmax before S_g replaces it
+            if (ok && g > 0) ok = mbar_wait(s_empty, static_cast<uint32_t>((g - 1) & 1), err, abort_flag, DEV_TIMEOUT_MMA);
             if (!ok) break;
             tc_fence_after();
-            issue_s(s_t, dq, dk0 + static_cast<uint64_t>((st_n * K_BYTES) >> 4));
+            issue_s(s_t, dq, dk0 + static_cast<uint64_t>(((g & 1) * K_BYTES) >> 4));
             umma_commit(s_full);
-            umma_commit(&k_empty[st_n]);
+            umma_commit(&k_empty[g & 1]);
+            if (j == it.nkv - 1) umma_commit(&q_empty[qs]);
+            if (g > 0 && !(ok = issue_pv_step(g - 1, prev_j, prev_n))) break;
+            prev_j = j;
+            prev_n = n;
           }
-          ok = mbar_wait(p_full, static_cast<uint32_t>(j & 1), err, abort_flag, DEV_TIMEOUT_MMA);
-          if (ok) ok = mbar_wait(&v_full[stage], phase, err, abort_flag, DEV_TIMEOUT_MMA);
-          if (!ok) break;
-          tc_fence_after();
-          issue_pv(o_t, p_t, dv0 + static_cast<uint64_t>((stage * V_BYTES) >> 4), j > 0);
-          umma_commit(o_done);
-          umma_commit(&v_empty[stage]);
-          stage = st_n;
-          phase = ph_n;
         }
+        if (ok && g > 0) issue_pv_step(g - 1, prev_j, prev_n);
       }
     }
   } else {
     regs_inc<REGS_SOFTMAX>();
     const int q = warp & 3;       // TMEM lane quarter
     const int r = q * 32 + lane;  // row inside the query block
-    const int qi = tile.q0 + r;
-    const int q_chunk = chunk > 0 ? qi / chunk : 0;
     const float sl2 = 0.125f * 1.4426950408889634f;  // 1/sqrt(64) * log2(e)
     const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
-    float m_ref = -INFINITY;  // reference max, scaled (log2) units
-    float l = 0.f;            // row sum of P relative to m_ref
     bool ok = true;
-    for (int j = 0; ok && j < nkv; ++j) {
-      ok = mbar_wait(s_full, static_cast<uint32_t>(j & 1), err, abort_flag, DEV_TIMEOUT_SOFTMAX);
+    int g = 0, n = 0;
+    for (int idx = blockIdx.x; ok && idx < n_items; idx += grid, ++n) {
+      const AttnItem it = load_item(tiles, idx, chunk);
+      const int len = it.t.seq_len;
+      const int qi = it.t.q0 + r;
+      const int q_chunk = chunk > 0 ? qi / chunk : 0;
+      float m_ref = -INFINITY;  // reference max, scaled (log2) units
+      float l = 0.f;            // row sum of P relative to m_ref
+      for (int j = 0; j < it.nkv; ++j, ++g) {
+        ok = mbar_wait(s_full, static_cast<uint32_t>(g & 1), err, abort_flag, DEV_TIMEOUT_SOFTMAX);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        tc_fence_after();
+        float s[128];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          float t[32];
+          tmem_ld32(t_lane + S_COL + c * 32, t);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) s[c * 32 + i] = t[i];
+        }
+        tmem_ld_wait();
+        // the S columns may now be overwritten by the next QK^T
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(s_empty);
+
+        // visible keys of this row form a prefix of the tile (key padding and
+        // the block-causal rule both cut at an upper bound): mask past it
+        const int key0 = j * 128;
+        int vis_end = len;
+        if (chunk > 0) vis_end = min(vis_end, (q_chunk + 1) * chunk);
+        const int nvalid = vis_end - key0;
+        if (nvalid < 128) {
+#pragma unroll
+          for (int c = 0; c < 128; ++c) s[c] = c < nvalid ? s[c] : -INFINITY;
+        }
+        float mx[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) mx[k] = fmaxf(s[k], s[k + 8]);
+#pragma unroll
+        for (int c = 16; c < 128; c += 16) {
+#pragma unroll
+          for (int k = 0; k < 8; ++k) mx[k] = max3(mx[k], s[c + k], s[c + 8 + k]);
+        }
+        const float rmax = max3(max3(mx[0], mx[1], mx[2]), max3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
+        const float m_cand = rmax * sl2;
+        const bool need = m_cand > m_ref + RESCALE_THRESHOLD;  // false when rmax == -inf
+        bool waited = false;
+        if (__any_sync(0xffffffffu, need)) {
+          const float new_ref = need ? m_cand : m_ref;
+          const float alpha = need ? ex2(m_ref - new_ref) : 1.0f;  // 0 from -inf
+          if (j > 0) {
+            // PV_{g-1} is the last update of O before this in-place rescale
+            ok = mbar_wait(o_done, static_cast<uint32_t>((g - 1) & 1), err, abort_flag, DEV_TIMEOUT_SOFTMAX);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) break;
+            tc_fence_after();
+            waited = true;
+#pragma unroll 1
+            for (int h = 0; h < 2; ++h) {
+              float t[32];
+              tmem_ld32(t_lane + O_COL + h * 32, t);
+              tmem_ld_wait();
+#pragma unroll
+              for (int i = 0; i < 32; ++i) t[i] *= alpha;
+              tmem_st32(t_lane + O_COL + h * 32, t);
+            }
+            tmem_st_wait();
+          }
+          l *= alpha;
+          m_ref = new_ref;
+        }
+        const float m_use = (m_ref == -INFINITY) ? 0.f : m_ref;
+        // p = 2^(s*scale - m) in fp32, row sum in fp32, P packed as fp16
+        // pairs; stored to TMEM in two 64-key halves
+        float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          uint32_t pk[32];
+          exp_chunk32(s + 64 * h, sl2, m_use, acc0, acc1, pk);
+          exp_chunk32(s + 64 * h + 32, sl2, m_use, acc0, acc1, pk + 16);
+          if (h == 0 && g > 0 && !waited) {
+            // PV_{g-1} (possibly the previous item's last) must have read
+            // P_{g-1} before P_g replaces it
+            ok = mbar_wait(o_done, static_cast<uint32_t>((g - 1) & 1), err, abort_flag, DEV_TIMEOUT_SOFTMAX);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) break;
+            tc_fence_after();
+          }
+          tmem_st32u(t_lane + P_COL + 32 * h, pk);
+        }
+        if (!ok) break;
+        l += (acc0.x + acc0.y) + (acc1.x + acc1.y);
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(p_full);
+      }
+      if (!ok) break;
+      // the item's O is final after its last PV (global step g - 1)
+      ok = mbar_wait(o_done, static_cast<uint32_t>((g - 1) & 1), err, abort_flag, DEV_TIMEOUT_SOFTMAX);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
-      float s[128];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float t[32];
-        tmem_ld32(t_lane + S_COL + c * 32, t);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) s[c * 32 + i] = t[i];
-      }
-      tmem_ld_wait();
-      // the S columns may now be overwritten by the next QK^T
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(s_empty);
-
-      // visible keys of this row form a prefix of the tile (key padding and the
-      // block-causal rule both cut at an upper bound): mask past it
-      const int key0 = j * 128;
-      int vis_end = len;
-      if (chunk > 0) vis_end = min(vis_end, (q_chunk + 1) * chunk);
-      const int nvalid = vis_end - key0;
-      if (nvalid < 128) {
-#pragma unroll
-        for (int c = 0; c < 128; ++c) s[c] = c < nvalid ? s[c] : -INFINITY;
-      }
-      float mx[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) mx[k] = fmaxf(s[k], s[k + 8]);
-#pragma unroll
-      for (int c = 16; c < 128; c += 16) {
-#pragma unroll
-        for (int k = 0; k < 8; ++k) mx[k] = max3(mx[k], s[c + k], s[c + 8 + k]);
-      }
-      const float rmax = max3(max3(mx[0], mx[1], mx[2]), max3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
-      const float m_cand = rmax * sl2;
-      const bool need = m_cand > m_ref + RESCALE_THRESHOLD;  // false when rmax == -inf
-      bool waited = false;
-      if (__any_sync(0xffffffffu, need)) {
-        const float new_ref = need ? m_cand : m_ref;
-        const float alpha = need ? ex2(m_ref - new_ref) : 1.0f;  // 0 from -inf
-        if (j > 0) {
-          // PV_{j-1} is the last update of O before this in-place rescale
-          ok = mbar_wait(o_done, static_cast<uint32_t>((j - 1) & 1), err, abort_flag, DEV_TIMEOUT_SOFTMAX);
-          ok = __all_sync(0xffffffffu, ok);
-          if (!ok) break;
-          tc_fence_after();
-          waited = true;
-#pragma unroll 1
-          for (int h = 0; h < 2; ++h) {
-            float t[32];
-            tmem_ld32(t_lane + O_COL + h * 32, t);
-            tmem_ld_wait();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) t[i] *= alpha;
-            tmem_st32(t_lane + O_COL + h * 32, t);
-          }
-          tmem_st_wait();
-        }
-        l *= alpha;
-        m_ref = new_ref;
-      }
-      const float m_use = (m_ref == -INFINITY) ? 0.f : m_ref;
-      // p = 2^(s*scale - m) in fp32, row sum in fp32, P packed as fp16 pairs;
-      // stored to TMEM in two 64-key halves
-      float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
+      float o[64];
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        uint32_t pk[32];
-        exp_chunk32(s + 64 * h, sl2, m_use, acc0, acc1, pk);
-        exp_chunk32(s + 64 * h + 32, sl2, m_use, acc0, acc1, pk + 16);
-        if (h == 0 && j > 0 && !waited) {
-          // PV_{j-1} must have read P_{j-1} before P_j replaces it
-          ok = mbar_wait(o_done, static_cast<uint32_t>((j - 1) & 1), err, abort_flag, DEV_TIMEOUT_SOFTMAX);
-          ok = __all_sync(0xffffffffu, ok);
-          if (!ok) break;
-          tc_fence_after();
-        }
-        tmem_st32u(t_lane + P_COL + 32 * h, pk);
+        float t[32];
+        tmem_ld32(t_lane + O_COL + h * 32, t);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[h * 32 + i] = t[i];
       }
-      if (!ok) break;
-      l += (acc0.x + acc0.y) + (acc1.x + acc1.y);
-      tmem_st_wait();
+      tmem_ld_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
-    }
-    if (ok && nkv > 0) {
-      ok = mbar_wait(o_done, static_cast<uint32_t>((nkv - 1) & 1), err, abort_flag, DEV_TIMEOUT_SOFTMAX);
-      ok = __all_sync(0xffffffffu, ok);
-      if (ok) {
-        tc_fence_after();
-        float o[64];
+      if (lane == 0) mbar_arrive(o_free);
+      const float inv = 1.0f / l;
+      if (r < it.nq) {
+        bf16* dst = out + static_cast<size_t>(it.t.seq_start + qi) * DIM + it.head * HDIM;
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          float t[32];
-          tmem_ld32(t_lane + O_COL + h * 32, t);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[h * 32 + i] = t[i];
-        }
-        tmem_ld_wait();
-        const float inv = 1.0f / l;
-        if (r < nq) {
-          bf16* dst = out + static_cast<size_t>(tile.seq_start + qi) * DIM + head * HDIM;
-#pragma unroll
-          for (int c = 0; c < 4; ++c)
-            st_global_v8(dst + 16 * c, pack_bf16x2(o[16 * c + 0] * inv, o[16 * c + 1] * inv),
-                         pack_bf16x2(o[16 * c + 2] * inv, o[16 * c + 3] * inv),
-                         pack_bf16x2(o[16 * c + 4] * inv, o[16 * c + 5] * inv),
-                         pack_bf16x2(o[16 * c + 6] * inv, o[16 * c + 7] * inv),
-                         pack_bf16x2(o[16 * c + 8] * inv, o[16 * c + 9] * inv),
-                         pack_bf16x2(o[16 * c + 10] * inv, o[16 * c + 11] * inv),
-                         pack_bf16x2(o[16 * c + 12] * inv, o[16 * c + 13] * inv),
-                         pack_bf16x2(o[16 * c + 14] * inv, o[16 * c + 15] * inv));
-        }
+        for (int c = 0; c < 4; ++c)
+          st_global_v8(dst + 16 * c, pack_bf16x2(o[16 * c + 0] * inv, o[16 * c + 1] * inv),
+                       pack_bf16x2(o[16 * c + 2] * inv, o[16 * c + 3] * inv),
+                       pack_bf16x2(o[16 * c + 4] * inv, o[16 * c + 5] * inv),
+                       pack_bf16x2(o[16 * c + 6] * inv, o[16 * c + 7] * inv),
+                       pack_bf16x2(o[16 * c + 8] * inv, o[16 * c + 9] * inv),
+                       pack_bf16x2(o[16 * c + 10] * inv, o[16 * c + 11] * inv),
+                       pack_bf16x2(o[16 * c + 12] * inv, o[16 * c + 13] * inv),
+                       pack_bf16x2(o[16 * c + 14] * inv, o[16 * c + 15] * inv));
       }
     }
   }
@@ -472,7 +508,10 @@ bool attention(const CUtensorMap& Q, const CUtensorMap& K, const CUtensorMap& V,
                int n_tiles, int chunk, bf16* out, int* err, cudaStream_t s) {
   if (n_tiles <= 0) return true;
   if (!attention_ready() || n_tiles > ATT_MAX_TILES) return false;
-  k_attention<<<dim3(HEADS, n_tiles), ATT_THREADS, ATT_SMEM, s>>>(Q, K, V, tiles, chunk, out, err);
+  // persistent: two CTAs per SM walk the (block, head) items
+  const int n_items = n_tiles * HEADS;
+  const int grid = n_items < 2 * num_sms() ? n_items : 2 * num_sms();
+  k_attention<<<grid, ATT_THREADS, ATT_SMEM, s>>>(Q, K, V, tiles, n_items, chunk, out, err);
   return true;
 }
 

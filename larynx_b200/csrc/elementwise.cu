@@ -251,17 +251,19 @@ __global__ void k_front_embed(const int* __restrict__ tok, int n, const float* _
   out[i] = table[static_cast<size_t>(id) * MEL + c];
 }
 
-// conv1: [80 -> 1024, k=4] over emb padded right by 3, then LeakyReLU(0.01).
-// emb [n][80] (time-major), w [1024][80][4], h [n][1024]
-__global__ void k_front_conv1(const float* __restrict__ emb, int n, const float* __restrict__ w,
+// conv1: [80 -> 1024, k=4] over the n_in rows of emb, zero beyond them, then
+// LeakyReLU(0.01); n_out outputs (n_out = n_in: the finalize path, right
+// padding 3; n_out = n_in - 3: the streaming path, the last 3 rows are context).
+// emb [n_in][80] (time-major), w [1024][80][4], h [n_out][1024]
+__global__ void k_front_conv1(const float* __restrict__ emb, int n_in, int n_out, const float* __restrict__ w,
                               const float* __restrict__ b, float* __restrict__ h) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n * DIM) return;
+  if (i >= n_out * DIM) return;
   const int t = i / DIM, o = i - t * DIM;
   float acc = b[o];
   for (int k = 0; k < 4; ++k) {
     const int ts = t + k;
-    if (ts >= n) break;
+    if (ts >= n_in) break;
     const float* e = emb + static_cast<size_t>(ts) * MEL;
     const float* wr = w + static_cast<size_t>(o) * MEL * 4 + k;
     for (int c = 0; c < MEL; ++c) acc = fmaf(wr[c * 4], e[c], acc);
@@ -410,8 +412,9 @@ void frontend_spk(const float* emb192, const float* w, const float* b, float* sp
 void frontend_embed(const int* tok, int n, const float* table, int vocab, float* out, cudaStream_t s) {
   if (n > 0) k_front_embed<<<blocks_for(static_cast<size_t>(n) * MEL, 256), 256, 0, s>>>(tok, n, table, vocab, out);
 }
-void frontend_conv1(const float* emb, int n, const float* w, const float* b, float* h, cudaStream_t s) {
-  if (n > 0) k_front_conv1<<<blocks_for(static_cast<size_t>(n) * DIM, 256), 256, 0, s>>>(emb, n, w, b, h);
+void frontend_conv1(const float* emb, int n_in, int n_out, const float* w, const float* b, float* h, cudaStream_t s) {
+  if (n_out > 0)
+    k_front_conv1<<<blocks_for(static_cast<size_t>(n_out) * DIM, 256), 256, 0, s>>>(emb, n_in, n_out, w, b, h);
 }
 void frontend_conv2(const float* h, const float* emb, int n, const float* w, const float* b, float* out,
                     cudaStream_t s) {

@@ -997,13 +997,24 @@ int lx_flow_estimator(lx_flow* h, int n_seq, const int32_t* lengths, const float
 int lx_flow_infer(lx_flow* h, const int32_t* prompt_tokens, int n_prompt, const int32_t* tokens, int n_tokens,
                   const float* prompt_feat, int mel_len1, const float* spk_embedding, const float* noise_z,
                   float* mel_out, size_t mel_cap, lx_flow_debug* debug) {
+  return lx_flow_infer_ex(h, prompt_tokens, n_prompt, tokens, n_tokens, prompt_feat, mel_len1, spk_embedding, noise_z,
+                          1, 0, mel_out, mel_cap, debug);
+}
+
+int lx_flow_infer_ex(lx_flow* h, const int32_t* prompt_tokens, int n_prompt, const int32_t* tokens, int n_tokens,
+                     const float* prompt_feat, int mel_len1, const float* spk_embedding, const float* noise_z,
+                     int finalize, int chunk, float* mel_out, size_t mel_cap, lx_flow_debug* debug) {
   if (!h) return LX_ERR_ARG;
+  if (chunk < 0) return h->fail(LX_ERR_ARG, "lx_flow_infer_ex: chunk < 0");
   if (!h->loaded) return h->fail(LX_ERR_STATE, "lx_flow_load_gguf has not succeeded");
   if (n_prompt < 0 || n_tokens < 0 || (n_prompt > 0 && !prompt_tokens) || (n_tokens > 0 && !tokens) ||
       !spk_embedding || !mel_out || mel_len1 < 0 || (mel_len1 > 0 && !prompt_feat))
     return h->fail(LX_ERR_ARG, "lx_flow_infer: bad argument");
   const int n_tok = n_prompt + n_tokens;
-  const int T = 2 * n_tok;
+  // streaming call: the last PRE_LOOKAHEAD tokens are PreLookahead context only
+  const int n_pre = finalize ? n_tok : n_tok - PRE_LOOKAHEAD;
+  if (!finalize && n_pre <= 0) return h->fail(LX_ERR_SHAPE, "a streaming call needs more tokens than the look-ahead");
+  const int T = 2 * n_pre;
   if (T <= 0 || mel_len1 > T) return h->fail(LX_ERR_SHAPE, "prompt_feat longer than the mel sequence");
   if (!noise_z && !h->noise_loaded) return h->fail(LX_ERR_STATE, "lx_flow_load_noise has not succeeded");
   if (!noise_z && T > LX_NOISE_MAX_FRAMES) return h->fail(LX_ERR_SHAPE, "sequence longer than the noise bank");
@@ -1037,9 +1048,9 @@ int lx_flow_infer(lx_flow* h, const int32_t* prompt_tokens, int n_prompt, const 
   // frontend (flow.cpp:134-182): spk affine, embedding, PreLookahead, x2 repeat, cond pad
   frontend_spk(h->f_spk_in, W.spk_w, W.spk_b, h->f_spk, s);
   frontend_embed(h->f_tok, n_tok, W.emb, 6561, h->f_emb, s);
-  frontend_conv1(h->f_emb, n_tok, W.pre1_w, W.pre1_b, h->f_h, s);
-  frontend_conv2(h->f_h, h->f_emb, n_tok, W.pre2_w, W.pre2_b, h->f_pre, s);
-  frontend_mu_cond(h->f_pre, n_tok, h->f_pf, mel_len1, h->f_mu, h->f_cond, s);
+  frontend_conv1(h->f_emb, n_tok, n_pre, W.pre1_w, W.pre1_b, h->f_h, s);
+  frontend_conv2(h->f_h, h->f_emb, n_pre, W.pre2_w, W.pre2_b, h->f_pre, s);
+  frontend_mu_cond(h->f_pre, n_pre, h->f_pf, mel_len1, h->f_mu, h->f_cond, s);
   h->launches += 5;
   // noise
   Plan p0 = make_plan(1, &T, true, 0, W.n_sched);
@@ -1067,7 +1078,7 @@ int lx_flow_infer(lx_flow* h, const int32_t* prompt_tokens, int n_prompt, const 
   b.spks = h->f_spk;
   b.noise = w.in_noise;
   b.mel_out = w.out_mel;
-  b.chunk = 0;
+  b.chunk = chunk;
   b.n_steps = 0;
   const bool want_stages =
       debug && (debug->input_proj || debug->input_embed || debug->blocks || debug->norm_out || debug->dphi);

@@ -24,6 +24,7 @@ constexpr int MOD_N = 6 * DIM;
 constexpr int CONV_K = 31;
 constexpr int CONV_G = 16;
 constexpr int COND_K = 3 * MEL;  // [cond, mu, spks] columns of the input projection
+constexpr int PRE_LOOKAHEAD = 3;  // PreLookaheadLayer look-ahead tokens
 
 // Number of SMs of the current device (cached per device).
 int num_sms();
@@ -148,7 +149,8 @@ void to_bf16(const float* src, bf16* dst, size_t n, cudaStream_t s);
 // ---- frontend (once per utterance) -----------------------------------------
 void frontend_spk(const float* emb192, const float* w, const float* b, float* spk80, cudaStream_t s);
 void frontend_embed(const int* tok, int n, const float* table, int vocab, float* out, cudaStream_t s);
-void frontend_conv1(const float* emb, int n, const float* w, const float* b, float* h, cudaStream_t s);
+// n_out = n_in (finalize: right zero padding) or n_in - 3 (streaming: the last 3 rows are context)
+void frontend_conv1(const float* emb, int n_in, int n_out, const float* w, const float* b, float* h, cudaStream_t s);
 void frontend_conv2(const float* h, const float* emb, int n, const float* w, const float* b, float* out,
                     cudaStream_t s);
 // mu[c][2t + r] = pre[t][c]; cond[c][t] = t < mel_len1 ? prompt_feat[t][c] : 0

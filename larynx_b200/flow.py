@@ -31,7 +31,9 @@ ERRORS = {1: "LX_ERR_ARG", 2: "LX_ERR_IO", 3: "LX_ERR_FORMAT", 4: "LX_ERR_SHAPE"
 EXPORTS = ("lx_flow_create", "lx_flow_destroy", "lx_flow_last_error", "lx_flow_load_gguf", "lx_flow_load_noise",
            "lx_flow_infer", "lx_flow_decode", "lx_flow_decode_device", "lx_flow_estimator",
            "lx_flow_launch_count", "lx_flow_op", "lx_flow_op_gemm", "lx_flow_op_attention",
-           "lx_flow_profile_decode", "lx_flow_op_attention_static")
+           "lx_flow_profile_decode", "lx_flow_op_attention_static", "lx_flow_infer_ex")
+
+PRE_LOOKAHEAD = 3  # PreLookaheadLayer look-ahead tokens (cosyvoice3.yaml pre_lookahead_len)
 
 KERNEL_CLASSES = ("in_proj", "conv_pos", "adaln", "qkv_gemm", "attention", "out_gemm", "ff1_gemm", "ff2_gemm",
                   "proj_out_gemm", "euler", "other")
@@ -73,6 +75,8 @@ def load_library(path: str = LIB_PATH):
     lib.lx_flow_load_noise.argtypes = [vp, ctypes.c_char_p]
     lib.lx_flow_infer.argtypes = [vp, _i32p, ctypes.c_int, _i32p, ctypes.c_int, _f32p, ctypes.c_int, _f32p, _f32p,
                                   _f32p, ctypes.c_size_t, ctypes.POINTER(LxFlowDebug)]
+    lib.lx_flow_infer_ex.argtypes = [vp, _i32p, ctypes.c_int, _i32p, ctypes.c_int, _f32p, ctypes.c_int, _f32p, _f32p,
+                                     ctypes.c_int, ctypes.c_int, _f32p, ctypes.c_size_t, ctypes.POINTER(LxFlowDebug)]
     lib.lx_flow_decode.argtypes = [vp, ctypes.POINTER(LxFlowBatch)]
     lib.lx_flow_decode_device.argtypes = [vp, ctypes.POINTER(LxFlowBatch), vp]
     lib.lx_flow_estimator.argtypes = [vp, ctypes.c_int, _i32p, _f32p, _f32p, _f32p, _f32p, ctypes.c_float,
@@ -86,7 +90,7 @@ def load_library(path: str = LIB_PATH):
     lib.lx_flow_op_gemm.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, vp, vp, vp, vp, vp]
     lib.lx_flow_op_attention.argtypes = [ctypes.c_int, _i32p, vp, vp, vp, vp, ctypes.c_int, vp]
     lib.lx_flow_op_attention_static.argtypes = [ctypes.c_int, _i32p, vp, vp, vp, vp, ctypes.c_int, vp]
-    for name in ("lx_flow_op_gemm", "lx_flow_op_attention", "lx_flow_op_attention_static", "lx_flow_create", "lx_flow_load_gguf", "lx_flow_load_noise", "lx_flow_infer", "lx_flow_decode",
+    for name in ("lx_flow_op_gemm", "lx_flow_op_attention", "lx_flow_op_attention_static", "lx_flow_infer_ex", "lx_flow_create", "lx_flow_load_gguf", "lx_flow_load_noise", "lx_flow_infer", "lx_flow_decode",
                  "lx_flow_decode_device", "lx_flow_estimator", "lx_flow_op"):
         getattr(lib, name).restype = ctypes.c_int
     _lib = lib
@@ -157,17 +161,27 @@ class FlowDecoder:
         return self._check(self._lib.lx_flow_load_noise(self._h, noise_path.encode()), "load_noise")
 
     def infer(self, prompt_tokens: Sequence[int], tokens: Sequence[int], prompt_feat, spk_embedding,
-              noise_z=None, debug: Optional[dict] = None) -> Optional[np.ndarray]:
+              noise_z=None, debug: Optional[dict] = None, finalize: bool = True,
+              chunk: int = 0) -> Optional[np.ndarray]:
         """FlowDecoder::infer (flow.h:61-77): token -> mel [80, MEL_T - mel_len1],
-        or None on failure.  noise_z [80, MEL_T] or None (slice of the loaded
-        bank).  ``debug`` (a dict) receives the step-1 stage captures."""
+        or None on failure.  noise_z [80, >= MEL_T] (its first MEL_T columns)
+        or None (slice of the loaded bank).  ``debug`` (a dict) receives the
+        step-1 stage captures.  ``finalize=False`` is the reference's streaming
+        call (flow_reference.py:546-548): the last 3 tokens are PreLookahead
+        context and MEL_T = 2 * (tokens - 3).  ``chunk`` > 0 applies the
+        block-causal chunk mask (upstream CosyVoice3's streaming attention)."""
         pt = np.ascontiguousarray(np.asarray(prompt_tokens, dtype=np.int32).reshape(-1))
         tk = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32).reshape(-1))
         pf = _f32(prompt_feat).reshape(-1, 80)
         spk = _f32(spk_embedding).reshape(-1)
-        T = 2 * (pt.size + tk.size)
-        nz = None if noise_z is None else _f32(noise_z).reshape(80, T)
-        out = np.empty((80, T - pf.shape[0]), np.float32)
+        T = 2 * (pt.size + tk.size - (0 if finalize else PRE_LOOKAHEAD))
+        nz = None
+        if noise_z is not None:
+            z = np.asarray(noise_z, np.float32).reshape(80, -1)
+            if z.shape[1] < T:
+                raise ValueError(f"noise_z has {z.shape[1]} frames, {T} needed")
+            nz = _f32(z[:, :T])
+        out = np.empty((80, max(T - pf.shape[0], 0)), np.float32)
         dbg = None
         bufs = {}
         if debug is not None:
@@ -176,9 +190,10 @@ class FlowDecoder:
                       "norm_out": (2, T, 1024), "dphi": (2, 80, T)}
             bufs = {k: np.empty(v, np.float32) for k, v in shapes.items()}
             dbg = LxFlowDebug(**{k: _ptr(v) for k, v in bufs.items()})
-        rc = self._lib.lx_flow_infer(self._h, pt.ctypes.data_as(_i32p), pt.size, tk.ctypes.data_as(_i32p), tk.size,
-                                     _ptr(pf), pf.shape[0], _ptr(spk), _ptr(nz), _ptr(out), out.size,
-                                     ctypes.byref(dbg) if dbg is not None else None)
+        rc = self._lib.lx_flow_infer_ex(self._h, pt.ctypes.data_as(_i32p), pt.size, tk.ctypes.data_as(_i32p),
+                                        tk.size, _ptr(pf), pf.shape[0], _ptr(spk), _ptr(nz), int(bool(finalize)),
+                                        int(chunk), _ptr(out), out.size,
+                                        ctypes.byref(dbg) if dbg is not None else None)
         if not self._check(rc, "infer"):
             return None
         if debug is not None:

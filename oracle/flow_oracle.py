@@ -460,27 +460,38 @@ def conv1d(x, w, b):
     return np.einsum("ock,kcl->ol", w, cols) + b[:, None]
 
 
-def prelookahead(W, tok_emb):
-    """PreLookaheadLayer, finalize=True (flow_reference.py:415-429).
-    tok_emb: [Tseq, 80] -> [Tseq, 80]."""
-    x = tok_emb.T                                                   # [80, T]
-    x = np.concatenate([x, np.zeros((MEL_DIM, PRE_LOOKAHEAD), x.dtype)], axis=1)
+def prelookahead(W, tok_emb, finalize=True):
+    """PreLookaheadLayer (flow_reference.py:406-429).  tok_emb: [Tseq, 80].
+    finalize=True: the sequence is right-padded with PRE_LOOKAHEAD zero rows and
+    all Tseq rows come out.  finalize=False (the streaming call,
+    flow_reference.py:546-548): the last PRE_LOOKAHEAD rows are look-ahead
+    context only (they replace the zero padding) and Tseq - PRE_LOOKAHEAD rows
+    come out, with the residual taken from the non-context rows."""
+    if finalize:
+        inp = tok_emb
+        x = np.concatenate([tok_emb.T, np.zeros((MEL_DIM, PRE_LOOKAHEAD), tok_emb.dtype)], axis=1)
+    else:
+        if tok_emb.shape[0] <= PRE_LOOKAHEAD:
+            raise ValueError("streaming PreLookahead needs more rows than the look-ahead context")
+        inp = tok_emb[:-PRE_LOOKAHEAD]
+        x = tok_emb.T                                               # inputs ++ context, no padding left
     y = conv1d(x, W["pre_lookahead_layer.conv1.weight"], W["pre_lookahead_layer.conv1.bias"])
     y = np.where(y >= 0, y, y * y.dtype.type(0.01))
     y = np.concatenate([np.zeros((DIM, 2), y.dtype), y], axis=1)
     y = conv1d(y, W["pre_lookahead_layer.conv2.weight"], W["pre_lookahead_layer.conv2.bias"])
-    return y.T + tok_emb
+    return y.T + inp
 
 
-def frontend(W, prompt_tokens, tokens, prompt_feat, spk_embedding, capture=None):
-    """Returns (mu [80, MEL_T], cond [80, MEL_T], spks [80])."""
+def frontend(W, prompt_tokens, tokens, prompt_feat, spk_embedding, capture=None, finalize=True):
+    """Returns (mu [80, MEL_T], cond [80, MEL_T], spks [80]).  MEL_T = 2 Tseq
+    (finalize) or 2 (Tseq - PRE_LOOKAHEAD) (streaming; flow_reference.py:531-555)."""
     e = np.asarray(spk_embedding, np.float32).reshape(-1)
     e = e / max(float(np.sqrt((e.astype(np.float64) ** 2).sum())), 1e-12)
     spk = (W["spk_embed_affine_layer.weight"] @ e.astype(np.float32) + W["spk_embed_affine_layer.bias"]).astype(np.float32)
     tok = np.concatenate([np.asarray(prompt_tokens), np.asarray(tokens)]).astype(np.int64)
     tok = np.maximum(tok, 0)
     emb = W["input_embedding.weight"][tok]                          # [Tseq, 80]
-    h = prelookahead(W, emb)
+    h = prelookahead(W, emb, finalize)
     h = np.repeat(h, TOKEN_MEL_RATIO, axis=0)                       # [MEL_T, 80]
     pf = np.asarray(prompt_feat, np.float32).reshape(-1, MEL_DIM)
     mel_t = h.shape[0]
@@ -491,13 +502,15 @@ def frontend(W, prompt_tokens, tokens, prompt_feat, spk_embedding, capture=None)
     return np.ascontiguousarray(h.T.astype(np.float32)), np.ascontiguousarray(cond.T), spk
 
 
-def infer(W, prompt_tokens, tokens, prompt_feat, spk_embedding, noise_z, capture=None):
-    """Token -> mel, whole-sequence path (FlowDecoder::infer 7-arg form,
-    src/flow/flow.cpp:110-287; flow_reference.py:598-665).
-    noise_z: [80, MEL_T].  Returns mel [80, MEL_T - mel_len1]."""
-    mu, cond, spk = frontend(W, prompt_tokens, tokens, prompt_feat, spk_embedding, capture)
+def infer(W, prompt_tokens, tokens, prompt_feat, spk_embedding, noise_z, capture=None, finalize=True):
+    """Token -> mel (FlowDecoder::infer 7-arg form, src/flow/flow.cpp:110-287;
+    flow_reference.py:531-563 / 598-665).  finalize=False is the streaming
+    call (flow_reference.py:546-548).  noise_z: [80, >= MEL_T] (the first MEL_T
+    columns are used, as the CFM slices its noise bank,
+    flow_reference.py:470).  Returns mel [80, MEL_T - mel_len1]."""
+    mu, cond, spk = frontend(W, prompt_tokens, tokens, prompt_feat, spk_embedding, capture, finalize)
     mel_len1 = np.asarray(prompt_feat).reshape(-1, MEL_DIM).shape[0]
-    z = np.asarray(noise_z, np.float32).reshape(MEL_DIM, -1)
+    z = np.asarray(noise_z, np.float32).reshape(MEL_DIM, -1)[:, : mu.shape[1]]
     x = solve_euler(W, z[None], mu[None], spk[None], cond[None], None, capture=capture)
     return x[0, :, mel_len1:]
 

@@ -18,6 +18,9 @@ reference checkout), loads the seeded synthetic weights of
   dit_chunk.npz     one estimator forward with a block-causal chunk mask
                     (chunk 50) through the streaming [B, T, T] mask input
                     (flow_reference.py:375-376)
+  flow_stream.npz   the streaming call (finalize=False: PreLookahead with the
+                    last 3 tokens as context) and the finalize=True output
+                    of the same inputs
   ops_fixture.npz   the fused-op pieces (AdaLN-Zero modulation, partial
                     rotary, GELU-tanh, Mish, time embedding + modulation
                     chunks for the 10-step schedule)
@@ -90,6 +93,36 @@ def make_flow_fixture(model):
     for i in KEEP_BLOCKS:
         out[f"dit_block{i}"] = cap["blocks"][i].numpy()
     np.savez_compressed(os.path.join(HERE, "flow_fixture.npz"), **out)
+
+
+def make_stream(model):
+    """The streaming (finalize=False) call of the reference's flow inference
+    (flow_reference.py:531-563): 4 prompt tokens + 12 tokens, the last 3
+    tokens acting as PreLookahead context; also the finalize=True output of
+    the same inputs."""
+    torch.manual_seed(4321)
+    P, T = 4, 12
+    prompt_tokens = torch.randint(0, fr.VOCAB, (1, P))
+    tokens = torch.randint(0, fr.VOCAB, (1, T))
+    prompt_feat = torch.randn(1, 2 * P, 80)
+    spk_embedding = torch.randn(1, 192)
+    args = (tokens, torch.tensor([T]), prompt_tokens, torch.tensor([P]), prompt_feat, torch.tensor([2 * P]),
+            spk_embedding)
+    with torch.inference_mode():
+        feat_s, _ = model.inference(*args, streaming=False, finalize=False)
+        feat_s2, _ = model.inference(*args, streaming=True, finalize=False)
+        feat_f, _ = model.inference(*args, streaming=False, finalize=True)
+        tok = torch.concat([prompt_tokens, tokens], dim=1)
+        emb = model.input_embedding(torch.clamp(tok, min=0))
+        pre = model.pre_lookahead_layer(emb[:, :-model.pre_lookahead_len], context=emb[:, -model.pre_lookahead_len:])
+    assert (feat_s - feat_s2).abs().max().item() < 1e-6  # streaming mask == padding mask at batch 1
+    mel_t = 2 * (P + T - 3)
+    np.savez_compressed(os.path.join(HERE, "flow_stream.npz"),
+                        prompt_tokens=prompt_tokens.numpy().astype(np.int32), tokens=tokens.numpy().astype(np.int32),
+                        prompt_feat=prompt_feat.numpy(), spk_embedding=spk_embedding.numpy(),
+                        noise_z=model.decoder.rand_noise[:, :, :2 * (P + T)].numpy(),
+                        prelookahead=pre.numpy(), feat_stream=feat_s.numpy(), feat_final=feat_f.numpy(),
+                        mel_t=np.int32(mel_t))
 
 
 def make_padded(model):
@@ -184,6 +217,7 @@ def main():
     make_chunk(model)
     make_padded(model)
     make_flow_fixture(model)
+    make_stream(model)
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             print(f, os.path.getsize(os.path.join(HERE, f)))

@@ -92,3 +92,20 @@ def test_euler_schedule():
     assert len(sched) == 10
     assert sched[0] == (0.0, float(ts[1]))
     assert abs(sum(dt for _, dt in sched) - 1.0) < 1e-6
+
+
+def test_streaming_call(weights):
+    """finalize=False: PreLookahead with the last 3 tokens as context
+    (flow_reference.py:546-548); also the finalize=True output of the same
+    inputs, which must differ from it."""
+    g = golden("flow_stream.npz")
+    cap = {}
+    args = (g["prompt_tokens"][0], g["tokens"][0], g["prompt_feat"][0], g["spk_embedding"][0], g["noise_z"][0])
+    mel_s = fo.infer(weights, *args, capture=cap, finalize=False)
+    assert rel_max(cap["prelookahead"], g["prelookahead"][0]) < TOL
+    assert mel_s.shape == g["feat_stream"][0].shape
+    assert rel_max(mel_s, g["feat_stream"][0]) < TOL
+    mel_f = fo.infer(weights, *args, finalize=True)
+    assert rel_max(mel_f, g["feat_final"][0]) < TOL
+    assert mel_f.shape[1] == mel_s.shape[1] + 2 * fo.PRE_LOOKAHEAD
+    assert np.abs(mel_f[:, :mel_s.shape[1]] - mel_s).max() > 1e-3   # the look-ahead context changes the result
