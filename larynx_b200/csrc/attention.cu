@@ -245,6 +245,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_launch_dependents();
+  pdl_wait();
 
   if (warp < 4) {
     regs_dec<REGS_PRODUCER>();
@@ -511,7 +513,7 @@ bool attention(const CUtensorMap& Q, const CUtensorMap& K, const CUtensorMap& V,
   // persistent: two CTAs per SM walk the (block, head) items
   const int n_items = n_tiles * HEADS;
   const int grid = n_items < 2 * num_sms() ? n_items : 2 * num_sms();
-  k_attention<<<grid, ATT_THREADS, ATT_SMEM, s>>>(Q, K, V, tiles, n_items, chunk, out, err);
+  launch_pdl(k_attention, dim3(grid), dim3(ATT_THREADS), ATT_SMEM, s, Q, K, V, tiles, n_items, chunk, out, err);
   return true;
 }
 

@@ -245,6 +245,20 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
 }
 
 // ---------------------------------------------------------------------------
+// Programmatic dependent launch.  pdl_launch_dependents lets the next kernel
+// of the stream launch now; pdl_wait blocks until the previous kernel of the
+// stream has finished and its memory is visible.  Every kernel of the decode
+// calls both before its first global access, so when launched with the
+// programmatic-serialization attribute (launch_pdl, opt-in) a dependent
+// kernel's launch and prologue (barrier init, TMEM allocation, descriptor
+// prefetch) overlap its predecessor's tail.  Both are no-ops otherwise.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// ---------------------------------------------------------------------------
 // 256-bit global stores: one full 32-byte sector per thread (the GEMM
 // epilogues write rows per thread, so a warp store touches 32 rows; a 16-byte
 // store would leave every sector half written by each instruction).

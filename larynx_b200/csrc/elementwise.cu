@@ -43,10 +43,12 @@ __device__ __forceinline__ void store4(bf16* p, float4 v) {
 // Two-pass statistics in registers (mean, then centred variance), biased
 // variance, eps 1e-6, then (x - mean) * rstd * (1 + scale) + shift.
 template <typename Tin, typename Tout>
-__global__ void __launch_bounds__(256) k_adaln(const Tin* __restrict__ x, Tout* __restrict__ y,
+__global__ void __launch_bounds__(512) k_adaln(const Tin* __restrict__ x, Tout* __restrict__ y,
                                                 const float* __restrict__ shift, const float* __restrict__ scale,
                                                 int R) {
-  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  pdl_launch_dependents();
+  pdl_wait();
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= R) return;
   const Tin* xr = x + static_cast<size_t>(row) * DIM;
@@ -85,6 +87,8 @@ __global__ void __launch_bounds__(256) k_adaln(const Tin* __restrict__ x, Tout* 
 //   x += dt * ((1 + cfg) * d_cond - cfg * d_uncond)
 __global__ void k_euler(float* __restrict__ xs, const float* __restrict__ dphi, const int2* __restrict__ rows,
                         bf16* __restrict__ xb, int F, float dt, float cfg) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= F * MEL) return;
   const int f = i / MEL, c = i - f * MEL;
@@ -304,26 +308,31 @@ __global__ void k_front_mu_cond(const float* __restrict__ pre, int n_tok, const 
 template <typename Tin>
 __global__ void k_gate_res(float* __restrict__ x, const Tin* __restrict__ y, const float* __restrict__ gate,
                            size_t n4) {
-  const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i >= n4) return;
-  const int c = static_cast<int>((i * 4) % DIM);
-  float4 xv = reinterpret_cast<float4*>(x)[i];
-  const float4 yv = load4(y + i * 4);
-  const float4 g = __ldg(reinterpret_cast<const float4*>(gate + c));
-  xv.x += g.x * yv.x;
-  xv.y += g.y * yv.y;
-  xv.z += g.z * yv.z;
-  xv.w += g.w * yv.w;
-  reinterpret_cast<float4*>(x)[i] = xv;
+  pdl_launch_dependents();
+  pdl_wait();
+  for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const int c = static_cast<int>((i * 4) % DIM);
+    float4 xv = reinterpret_cast<float4*>(x)[i];
+    const float4 yv = load4(y + i * 4);
+    const float4 g = __ldg(reinterpret_cast<const float4*>(gate + c));
+    xv.x += g.x * yv.x;
+    xv.y += g.y * yv.y;
+    xv.z += g.z * yv.z;
+    xv.w += g.w * yv.w;
+    reinterpret_cast<float4*>(x)[i] = xv;
+  }
 }
 
 // Partial rotary of one row per warp: lanes 0..31 rotate pair i = lane of
 // channels (2i, 2i+1); every lane also copies its share of channels 64..1023.
 template <typename Tin>
-__global__ void __launch_bounds__(256) k_rotary(const Tin* __restrict__ x, float* __restrict__ y,
+__global__ void __launch_bounds__(512) k_rotary(const Tin* __restrict__ x, float* __restrict__ y,
                                                  const int* __restrict__ pos, const float2* __restrict__ rope,
                                                  int R) {
-  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  pdl_launch_dependents();
+  pdl_wait();
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= R) return;
   const Tin* xr = x + static_cast<size_t>(row) * DIM;
@@ -345,26 +354,37 @@ __global__ void __launch_bounds__(256) k_rotary(const Tin* __restrict__ x, float
 
 template <typename Tin>
 __global__ void k_gelu(const Tin* __restrict__ x, float* __restrict__ y, size_t n4) {
-  const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i >= n4) return;
-  float4 v = load4(x + i * 4);
-  v.x = gelu_tanh_f(v.x);
-  v.y = gelu_tanh_f(v.y);
-  v.z = gelu_tanh_f(v.z);
-  v.w = gelu_tanh_f(v.w);
-  reinterpret_cast<float4*>(y)[i] = v;
+  pdl_launch_dependents();
+  pdl_wait();
+  for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    float4 v = load4(x + i * 4);
+    v.x = gelu_tanh_fast(v.x);
+    v.y = gelu_tanh_fast(v.y);
+    v.z = gelu_tanh_fast(v.z);
+    v.w = gelu_tanh_fast(v.w);
+    reinterpret_cast<float4*>(y)[i] = v;
+  }
 }
 
 inline unsigned blocks_for(size_t n, unsigned t) { return static_cast<unsigned>((n + t - 1) / t); }
 
+// Grid of a grid-stride element-wise kernel: 4 blocks of 256 threads per SM
+// at most, fewer when the work is smaller.
+inline unsigned stride_grid(size_t n4) {
+  const size_t want = (n4 + 255) / 256;
+  const size_t cap = static_cast<size_t>(4) * num_sms();
+  return static_cast<unsigned>(want < cap ? (want ? want : 1) : cap);
+}
+
 }  // namespace
 
 void adaln_rows(const float* x, bf16* y, const float* shift, const float* scale, int R, cudaStream_t s) {
-  if (R > 0) k_adaln<float, bf16><<<(R + 7) / 8, 256, 0, s>>>(x, y, shift, scale, R);
+  if (R > 0) launch_pdl(k_adaln<float, bf16>, dim3((R + rows_per_block(R) - 1) / rows_per_block(R)), dim3(32 * rows_per_block(R)), 0, s, x, y, shift, scale, R);
 }
 void euler_update(float* xs, const float* dphi, const int2* frame_rows, bf16* xb, int F, float dt, float cfg,
                   cudaStream_t s) {
-  if (F > 0) k_euler<<<blocks_for(static_cast<size_t>(F) * MEL, 256), 256, 0, s>>>(xs, dphi, frame_rows, xb, F, dt, cfg);
+  if (F > 0) launch_pdl(k_euler, dim3(blocks_for(static_cast<size_t>(F) * MEL, 256)), dim3(256), 0, s, xs, dphi, frame_rows, xb, F, dt, cfg);
 }
 void init_state(float* xs, const float* noise, const int2* frame_rows, const int2* frame_src, bf16* xb, int F,
                 cudaStream_t s) {
@@ -427,30 +447,30 @@ void frontend_mu_cond(const float* pre, int n_tok, const float* prompt_feat, int
 }
 
 void op_adaln_f32(const float* x, float* y, const float* shift, const float* scale, int R, cudaStream_t s) {
-  if (R > 0) k_adaln<float, float><<<(R + 7) / 8, 256, 0, s>>>(x, y, shift, scale, R);
+  if (R > 0) launch_pdl(k_adaln<float, float>, dim3((R + rows_per_block(R) - 1) / rows_per_block(R)), dim3(32 * rows_per_block(R)), 0, s, x, y, shift, scale, R);
 }
 void op_adaln_bf16(const bf16* x, float* y, const float* shift, const float* scale, int R, cudaStream_t s) {
-  if (R > 0) k_adaln<bf16, float><<<(R + 7) / 8, 256, 0, s>>>(x, y, shift, scale, R);
+  if (R > 0) launch_pdl(k_adaln<bf16, float>, dim3((R + rows_per_block(R) - 1) / rows_per_block(R)), dim3(32 * rows_per_block(R)), 0, s, x, y, shift, scale, R);
 }
 void op_gate_res_f32(float* x, const float* y, const float* gate, int R, cudaStream_t s) {
   const size_t n4 = static_cast<size_t>(R) * DIM / 4;
-  if (n4) k_gate_res<float><<<blocks_for(n4, 256), 256, 0, s>>>(x, y, gate, n4);
+  if (n4) launch_pdl(k_gate_res<float>, dim3(stride_grid(n4)), dim3(256), 0, s, x, y, gate, n4);
 }
 void op_gate_res_bf16(float* x, const bf16* y, const float* gate, int R, cudaStream_t s) {
   const size_t n4 = static_cast<size_t>(R) * DIM / 4;
-  if (n4) k_gate_res<bf16><<<blocks_for(n4, 256), 256, 0, s>>>(x, y, gate, n4);
+  if (n4) launch_pdl(k_gate_res<bf16>, dim3(stride_grid(n4)), dim3(256), 0, s, x, y, gate, n4);
 }
 void op_rotary_f32(const float* x, float* y, const int* pos, const float2* rope, int R, cudaStream_t s) {
-  if (R > 0) k_rotary<float><<<(R + 7) / 8, 256, 0, s>>>(x, y, pos, rope, R);
+  if (R > 0) launch_pdl(k_rotary<float>, dim3((R + rows_per_block(R) - 1) / rows_per_block(R)), dim3(32 * rows_per_block(R)), 0, s, x, y, pos, rope, R);
 }
 void op_rotary_bf16(const bf16* x, float* y, const int* pos, const float2* rope, int R, cudaStream_t s) {
-  if (R > 0) k_rotary<bf16><<<(R + 7) / 8, 256, 0, s>>>(x, y, pos, rope, R);
+  if (R > 0) launch_pdl(k_rotary<bf16>, dim3((R + rows_per_block(R) - 1) / rows_per_block(R)), dim3(32 * rows_per_block(R)), 0, s, x, y, pos, rope, R);
 }
 void op_gelu_f32(const float* x, float* y, size_t n, cudaStream_t s) {
-  if (n >= 4) k_gelu<float><<<blocks_for(n / 4, 256), 256, 0, s>>>(x, y, n / 4);
+  if (n >= 4) launch_pdl(k_gelu<float>, dim3(stride_grid(n / 4)), dim3(256), 0, s, x, y, n / 4);
 }
 void op_gelu_bf16(const bf16* x, float* y, size_t n, cudaStream_t s) {
-  if (n >= 4) k_gelu<bf16><<<blocks_for(n / 4, 256), 256, 0, s>>>(x, y, n / 4);
+  if (n >= 4) launch_pdl(k_gelu<bf16>, dim3(stride_grid(n / 4)), dim3(256), 0, s, x, y, n / 4);
 }
 
 }  // namespace lx

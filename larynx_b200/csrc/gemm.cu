@@ -26,6 +26,30 @@ int num_sms() {
   return cache[dev];
 }
 
+bool pdl_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    // opt-in: measured on the 64-utterance decode PDL costs ~2% of throughput
+    // (dependent CTAs park on SMs the running kernel's tail could use) and
+    // saves ~1 ms of the single-utterance latency
+    const char* e = getenv("LX_FLOW_PDL");
+    on = (e && e[0] == '1') ? 1 : 0;
+  }
+  return on != 0;
+}
+
+int rows_per_block(int R) {
+  static int fixed = -1;
+  if (fixed < 0) {
+    const char* e = getenv("LX_FLOW_ROWS_PER_BLOCK");
+    fixed = e ? atoi(e) : 8;
+  }
+  if (fixed > 0) return fixed > 16 ? 16 : fixed;
+  // 0: up to 16, few enough that a small batch spreads over every SM in one wave
+  const int per_sm = (R + num_sms() - 1) / num_sms();
+  return per_sm < 1 ? 1 : per_sm > 16 ? 16 : per_sm;
+}
+
 typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                     const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                     CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -271,7 +295,7 @@ static void launch(const CUtensorMap& A, const CUtensorMap& B, int M, int N, int
   if (tiles < grid) grid = tiles;
   if (grid <= 0) return;
   GemmShape sh{M, N, K, b_off, err};
-  k_gemm<BN, STAGES, MODE, Epi><<<grid, gemm_threads(MODE), smem, s>>>(A, B, X ? *X : A, sh, epi);
+  launch_pdl(k_gemm<BN, STAGES, MODE, Epi>, dim3(grid), dim3(gemm_threads(MODE)), smem, s, A, B, X ? *X : A, sh, epi);
 }
 
 // CTA-pair launch: persistent grid of up to num_sms() / 2 clusters of 2.
@@ -291,7 +315,8 @@ static void launch_pair(const CUtensorMap& A, const CUtensorMap& B, int M, int N
   if (tiles < pairs) pairs = tiles;
   if (pairs <= 0) return;
   GemmShape sh{M, N, K, b_off, err};
-  k_gemm2<STAGES, RES, XS, Epi><<<2 * pairs, GEMM2_THREADS, smem, s>>>(A, B, X ? *X : A, sh, epi);
+  launch_pdl(k_gemm2<STAGES, RES, XS, Epi>, dim3(2 * pairs), dim3(GEMM2_THREADS), smem, s, A, B, X ? *X : A, sh,
+             epi);
 }
 
 template <class Epi>

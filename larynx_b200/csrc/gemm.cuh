@@ -136,6 +136,8 @@ __global__ void __launch_bounds__(gemm_threads(MODE), 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_launch_dependents();
+  pdl_wait();
 
   const int tiles_n = (sh.N + BN - 1) / BN;
   const int tiles_m = (sh.M + GEMM_BM - 1) / GEMM_BM;

@@ -265,6 +265,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM2_THREADS, 1)
   cluster_sync_all();  // barrier inits and the TMEM address visible pair-wide
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_launch_dependents();
+  pdl_wait();
 
   const int tiles_n = sh.N / G2_BN;
   const int tiles_m = (sh.M + G2_BM - 1) / G2_BM;

@@ -29,6 +29,35 @@ constexpr int PRE_LOOKAHEAD = 3;  // PreLookaheadLayer look-ahead tokens
 // Number of SMs of the current device (cached per device).
 int num_sms();
 
+// Launch with programmatic stream serialization (see pdl_wait in common.cuh):
+// the kernel may start while the previous kernel of the stream drains, and
+// waits for it inside before touching memory.
+// LX_FLOW_PDL=1 in the environment turns the attribute on (off by default).
+bool pdl_enabled();
+// Rows per block of the warp-per-row kernels (LX_FLOW_ROWS_PER_BLOCK, default
+// 8; 0 = as many as spread a small batch over every SM in one wave, <= 16).
+int rows_per_block(int R);
+
+template <typename... KArgs, typename... Args>
+inline void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                       Args... args) {
+  if (!pdl_enabled()) {
+    kernel<<<grid, block, smem, s>>>(static_cast<KArgs>(args)...);
+    return;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // 2-D tensor map over 16-bit elements (bf16, or fp16 data: TMA copies bits):
 // `rows` x `cols` elements, row stride `ld` elements, box = box_rows x
 // box_cols (box_cols * 2 == 128 selects the 128B swizzle).
