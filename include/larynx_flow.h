@@ -68,6 +68,18 @@ const char* lx_flow_last_error(const lx_flow* h);
  * cosine 10-step schedule.  Idempotent like the reference. */
 int lx_flow_load_gguf(lx_flow* h, const char* path);
 
+/* Pre-laid-out weight cache (the flow.gguf -> device layout step done once;
+ * the reference re-reads and converts the GGUF on every load,
+ * src/flow/gguf.cpp:30-136).  lx_flow_save_layout writes the loaded model's
+ * device layout (bf16 stacked projections, conv slices, rotary and
+ * default-schedule modulation tables; ~1 GB) to `path`;
+ * lx_flow_load_layout loads such a file instead of lx_flow_load_gguf (plain
+ * copies: no GGUF parsing, conversion or table computation).  The file is
+ * tied to this library's layout constants: another version returns
+ * LX_ERR_FORMAT. */
+int lx_flow_save_layout(lx_flow* h, const char* path);
+int lx_flow_load_layout(lx_flow* h, const char* path);
+
 /* Replaces FlowDecoder::load_noise (include/larynx/flow/flow.h:55;
  * src/flow/flow.cpp:70-108): the FNSE seed-noise bank (u32 magic 0x45534E46,
  * u32 version 1, u32 mel_dim 80, u64 max_frames 15000, f32[80][15000]). */

@@ -73,6 +73,7 @@ struct lx_flow {
   int* d_err = nullptr;
   uint64_t launches = 0;
   bool loaded = false;
+  std::string gguf_path;     // the flow.gguf the model came from (recorded in layout files)
   std::vector<float> noise;  // [80][15000]
   bool noise_loaded = false;
   Model W;
@@ -824,6 +825,48 @@ int lx_flow_load_gguf(lx_flow* h, const char* path) {
     h->W = Model();
     return rc;
   }
+  h->gguf_path = path;
+  h->loaded = true;
+  return LX_OK;
+}
+
+int lx_flow_save_layout(lx_flow* h, const char* path) {
+  if (!h || !path) return LX_ERR_ARG;
+  if (!h->loaded) return h->fail(LX_ERR_STATE, "no model loaded");
+  CK(cudaSetDevice(h->device));
+  CK(cudaStreamSynchronize(h->stream));
+  std::string msg;
+  const int rc = save_layout_file(h->W, h->gguf_path, path, &msg);
+  return rc ? h->fail(rc, msg) : LX_OK;
+}
+
+int lx_flow_load_layout(lx_flow* h, const char* path) {
+  if (!h || !path) return LX_ERR_ARG;
+  if (h->loaded) return LX_OK;
+  CK(cudaSetDevice(h->device));
+  Model& W = h->W;
+  std::string msg;
+  int rc = load_layout_file(W, h->allocs, path, &msg);
+  if (!rc)
+    rc = (dev_alloc(h, &W.mod_x, static_cast<size_t>(DEPTH) * MOD_N)) ||
+                 (dev_alloc(h, &W.mod_final_x, 2 * DIM)) || (dev_alloc(h, &W.temb_x, DIM)) ||
+                 (dev_alloc(h, &W.tscratch, 16 * 256 + 16 * DIM + 64))
+             ? LX_ERR_OOM
+             : LX_OK;
+  else
+    h->fail(rc, msg);
+  if (!rc) {
+    make_schedule(N_STEPS_DEFAULT, W.sched_t, W.sched_dt);
+    W.n_sched = N_STEPS_DEFAULT;
+    rc = build_model_maps(h);
+  }
+  if (rc) {
+    for (void* p : h->allocs) cudaFree(p);
+    h->allocs.clear();
+    h->W = Model();
+    return rc;
+  }
+  h->gguf_path.clear();
   h->loaded = true;
   return LX_OK;
 }

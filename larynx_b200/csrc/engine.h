@@ -47,6 +47,13 @@ struct Model {
   CUtensorMap tm_wconv[2], tm_wout;
 };
 
+// Pre-laid-out weight cache (layout.cu): write the device layout of a loaded
+// model to `path`, or allocate (recorded in `allocs`) and fill the weight,
+// rotary and default-schedule modulation buffers from such a file.  They
+// return an LX_* status and put the message in *msg on failure.
+int save_layout_file(Model& W, const std::string& gguf_path, const char* path, std::string* msg);
+int load_layout_file(Model& W, std::vector<void*>& allocs, const char* path, std::string* msg);
+
 // Packed variable-length layout of one batch.
 struct Plan {
   int n_seq = 0;

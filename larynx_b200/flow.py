@@ -31,7 +31,8 @@ ERRORS = {1: "LX_ERR_ARG", 2: "LX_ERR_IO", 3: "LX_ERR_FORMAT", 4: "LX_ERR_SHAPE"
 EXPORTS = ("lx_flow_create", "lx_flow_destroy", "lx_flow_last_error", "lx_flow_load_gguf", "lx_flow_load_noise",
            "lx_flow_infer", "lx_flow_decode", "lx_flow_decode_device", "lx_flow_estimator",
            "lx_flow_launch_count", "lx_flow_op", "lx_flow_op_gemm", "lx_flow_op_attention",
-           "lx_flow_profile_decode", "lx_flow_op_attention_static", "lx_flow_infer_ex")
+           "lx_flow_profile_decode", "lx_flow_op_attention_static", "lx_flow_infer_ex", "lx_flow_save_layout",
+           "lx_flow_load_layout")
 
 PRE_LOOKAHEAD = 3  # PreLookaheadLayer look-ahead tokens (cosyvoice3.yaml pre_lookahead_len)
 
@@ -73,6 +74,8 @@ def load_library(path: str = LIB_PATH):
     lib.lx_flow_last_error.restype = ctypes.c_char_p
     lib.lx_flow_load_gguf.argtypes = [vp, ctypes.c_char_p]
     lib.lx_flow_load_noise.argtypes = [vp, ctypes.c_char_p]
+    lib.lx_flow_save_layout.argtypes = [vp, ctypes.c_char_p]
+    lib.lx_flow_load_layout.argtypes = [vp, ctypes.c_char_p]
     lib.lx_flow_infer.argtypes = [vp, _i32p, ctypes.c_int, _i32p, ctypes.c_int, _f32p, ctypes.c_int, _f32p, _f32p,
                                   _f32p, ctypes.c_size_t, ctypes.POINTER(LxFlowDebug)]
     lib.lx_flow_infer_ex.argtypes = [vp, _i32p, ctypes.c_int, _i32p, ctypes.c_int, _f32p, ctypes.c_int, _f32p, _f32p,
@@ -90,7 +93,8 @@ def load_library(path: str = LIB_PATH):
     lib.lx_flow_op_gemm.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, vp, vp, vp, vp, vp]
     lib.lx_flow_op_attention.argtypes = [ctypes.c_int, _i32p, vp, vp, vp, vp, ctypes.c_int, vp]
     lib.lx_flow_op_attention_static.argtypes = [ctypes.c_int, _i32p, vp, vp, vp, vp, ctypes.c_int, vp]
-    for name in ("lx_flow_op_gemm", "lx_flow_op_attention", "lx_flow_op_attention_static", "lx_flow_infer_ex", "lx_flow_create", "lx_flow_load_gguf", "lx_flow_load_noise", "lx_flow_infer", "lx_flow_decode",
+    for name in ("lx_flow_op_gemm", "lx_flow_op_attention", "lx_flow_op_attention_static", "lx_flow_infer_ex",
+                 "lx_flow_save_layout", "lx_flow_load_layout", "lx_flow_create", "lx_flow_load_gguf", "lx_flow_load_noise", "lx_flow_infer", "lx_flow_decode",
                  "lx_flow_decode_device", "lx_flow_estimator", "lx_flow_op"):
         getattr(lib, name).restype = ctypes.c_int
     _lib = lib
@@ -155,6 +159,14 @@ class FlowDecoder:
     def load(self, gguf_path: str) -> bool:
         """FlowDecoder::load (flow.h:48)."""
         return self._check(self._lib.lx_flow_load_gguf(self._h, gguf_path.encode()), "load")
+
+    def save_layout(self, path: str) -> bool:
+        """Write the loaded model's device layout (pre-laid-out weight cache)."""
+        return self._check(self._lib.lx_flow_save_layout(self._h, path.encode()), "save_layout")
+
+    def load_layout(self, path: str) -> bool:
+        """Load a file written by save_layout instead of a flow.gguf."""
+        return self._check(self._lib.lx_flow_load_layout(self._h, path.encode()), "load_layout")
 
     def load_noise(self, noise_path: str) -> bool:
         """FlowDecoder::load_noise (flow.h:55)."""
