@@ -310,18 +310,17 @@ __global__ void k_gate_res(float* __restrict__ x, const Tin* __restrict__ y, con
                            size_t n4) {
   pdl_launch_dependents();
   pdl_wait();
-  for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4;
-       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
-    const int c = static_cast<int>((i * 4) % DIM);
-    float4 xv = reinterpret_cast<float4*>(x)[i];
-    const float4 yv = load4(y + i * 4);
-    const float4 g = __ldg(reinterpret_cast<const float4*>(gate + c));
-    xv.x += g.x * yv.x;
-    xv.y += g.y * yv.y;
-    xv.z += g.z * yv.z;
-    xv.w += g.w * yv.w;
-    reinterpret_cast<float4*>(x)[i] = xv;
-  }
+  const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n4) return;
+  const int c = static_cast<int>((i * 4) % DIM);
+  float4 xv = reinterpret_cast<float4*>(x)[i];
+  const float4 yv = load4(y + i * 4);
+  const float4 g = __ldg(reinterpret_cast<const float4*>(gate + c));
+  xv.x += g.x * yv.x;
+  xv.y += g.y * yv.y;
+  xv.z += g.z * yv.z;
+  xv.w += g.w * yv.w;
+  reinterpret_cast<float4*>(x)[i] = xv;
 }
 
 // Partial rotary of one row per warp: lanes 0..31 rotate pair i = lane of
@@ -356,26 +355,17 @@ template <typename Tin>
 __global__ void k_gelu(const Tin* __restrict__ x, float* __restrict__ y, size_t n4) {
   pdl_launch_dependents();
   pdl_wait();
-  for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4;
-       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
-    float4 v = load4(x + i * 4);
-    v.x = gelu_tanh_fast(v.x);
-    v.y = gelu_tanh_fast(v.y);
-    v.z = gelu_tanh_fast(v.z);
-    v.w = gelu_tanh_fast(v.w);
-    reinterpret_cast<float4*>(y)[i] = v;
-  }
+  const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n4) return;
+  float4 v = load4(x + i * 4);
+  v.x = gelu_tanh_fast(v.x);
+  v.y = gelu_tanh_fast(v.y);
+  v.z = gelu_tanh_fast(v.z);
+  v.w = gelu_tanh_fast(v.w);
+  reinterpret_cast<float4*>(y)[i] = v;
 }
 
 inline unsigned blocks_for(size_t n, unsigned t) { return static_cast<unsigned>((n + t - 1) / t); }
-
-// Grid of a grid-stride element-wise kernel: 4 blocks of 256 threads per SM
-// at most, fewer when the work is smaller.
-inline unsigned stride_grid(size_t n4) {
-  const size_t want = (n4 + 255) / 256;
-  const size_t cap = static_cast<size_t>(4) * num_sms();
-  return static_cast<unsigned>(want < cap ? (want ? want : 1) : cap);
-}
 
 }  // namespace
 
@@ -454,11 +444,11 @@ void op_adaln_bf16(const bf16* x, float* y, const float* shift, const float* sca
 }
 void op_gate_res_f32(float* x, const float* y, const float* gate, int R, cudaStream_t s) {
   const size_t n4 = static_cast<size_t>(R) * DIM / 4;
-  if (n4) launch_pdl(k_gate_res<float>, dim3(stride_grid(n4)), dim3(256), 0, s, x, y, gate, n4);
+  if (n4) launch_pdl(k_gate_res<float>, dim3(blocks_for(n4, 256)), dim3(256), 0, s, x, y, gate, n4);
 }
 void op_gate_res_bf16(float* x, const bf16* y, const float* gate, int R, cudaStream_t s) {
   const size_t n4 = static_cast<size_t>(R) * DIM / 4;
-  if (n4) launch_pdl(k_gate_res<bf16>, dim3(stride_grid(n4)), dim3(256), 0, s, x, y, gate, n4);
+  if (n4) launch_pdl(k_gate_res<bf16>, dim3(blocks_for(n4, 256)), dim3(256), 0, s, x, y, gate, n4);
 }
 void op_rotary_f32(const float* x, float* y, const int* pos, const float2* rope, int R, cudaStream_t s) {
   if (R > 0) launch_pdl(k_rotary<float>, dim3((R + rows_per_block(R) - 1) / rows_per_block(R)), dim3(32 * rows_per_block(R)), 0, s, x, y, pos, rope, R);
@@ -467,10 +457,10 @@ void op_rotary_bf16(const bf16* x, float* y, const int* pos, const float2* rope,
   if (R > 0) launch_pdl(k_rotary<bf16>, dim3((R + rows_per_block(R) - 1) / rows_per_block(R)), dim3(32 * rows_per_block(R)), 0, s, x, y, pos, rope, R);
 }
 void op_gelu_f32(const float* x, float* y, size_t n, cudaStream_t s) {
-  if (n >= 4) launch_pdl(k_gelu<float>, dim3(stride_grid(n / 4)), dim3(256), 0, s, x, y, n / 4);
+  if (n >= 4) launch_pdl(k_gelu<float>, dim3(blocks_for(n / 4, 256)), dim3(256), 0, s, x, y, n / 4);
 }
 void op_gelu_bf16(const bf16* x, float* y, size_t n, cudaStream_t s) {
-  if (n >= 4) launch_pdl(k_gelu<bf16>, dim3(stride_grid(n / 4)), dim3(256), 0, s, x, y, n / 4);
+  if (n >= 4) launch_pdl(k_gelu<bf16>, dim3(blocks_for(n / 4, 256)), dim3(256), 0, s, x, y, n / 4);
 }
 
 }  // namespace lx
