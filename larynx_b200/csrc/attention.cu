@@ -352,11 +352,27 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
       const int q_chunk = chunk > 0 ? qi / chunk : 0;
       float m_ref = -INFINITY;  // reference max, scaled (log2) units
       float l = 0.f;            // row sum of P relative to m_ref
+      // a warp whose 32 rows all lie past the block's last query only keeps
+      // the barrier protocol: its P rows feed O rows that are never stored
+      const bool live = __any_sync(0xffffffffu, r < it.nq);
       for (int j = 0; j < it.nkv; ++j, ++g) {
         ok = mbar_wait(s_full, static_cast<uint32_t>(g & 1), err, abort_flag, DEV_TIMEOUT_SOFTMAX);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
         tc_fence_after();
+        if (!live) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(s_empty);
+          // P_g may only be announced after PV_{g-1} retired, as on the live path
+          if (g > 0) {
+            ok = mbar_wait(o_done, static_cast<uint32_t>((g - 1) & 1), err, abort_flag, DEV_TIMEOUT_SOFTMAX);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) break;
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(p_full);
+          continue;
+        }
         float s[128];
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
@@ -381,6 +397,9 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
 #pragma unroll
           for (int c = 0; c < 128; ++c) s[c] = c < nvalid ? s[c] : -INFINITY;
         }
+        // 32-key chunks past every row's visible prefix hold p = 0 exactly:
+        // they are stored as zeros without running their exponentials
+        const int nv_warp = __reduce_max_sync(0xffffffffu, nvalid);
         float mx[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k) mx[k] = fmaxf(s[k], s[k + 8]);
@@ -424,8 +443,18 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           uint32_t pk[32];
-          exp_chunk32(s + 64 * h, sl2, m_use, acc0, acc1, pk);
-          exp_chunk32(s + 64 * h + 32, sl2, m_use, acc0, acc1, pk + 16);
+          if (64 * h < nv_warp) {
+            exp_chunk32(s + 64 * h, sl2, m_use, acc0, acc1, pk);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) pk[i] = 0u;
+          }
+          if (64 * h + 32 < nv_warp) {
+            exp_chunk32(s + 64 * h + 32, sl2, m_use, acc0, acc1, pk + 16);
+          } else {
+#pragma unroll
+            for (int i = 16; i < 32; ++i) pk[i] = 0u;
+          }
           if (h == 0 && g > 0 && !waited) {
             // PV_{g-1} (possibly the previous item's last) must have read
             // P_{g-1} before P_g replaces it
@@ -449,6 +478,11 @@ __global__ void __launch_bounds__(ATT_THREADS, 2)
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
+      if (!live) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(o_free);
+        continue;
+      }
       float o[64];
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
