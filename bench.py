@@ -307,6 +307,55 @@ def bench_cfg4(dec, dev, stream, streams=256, iters=3):
     return out
 
 
+def bench_hift(dev, T=1000, iters=5):
+    """HiFT vocoder (the stage after the Flow decoder) on one 20 s utterance:
+    mel [80][T] in HBM -> 24 kHz audio, device-timed, synthetic weights and
+    source bank.  The conv network runs in float32 on the CUDA cores; its
+    FLOP rate is reported against the nominal FP32 CUDA-core peak."""
+    import tempfile
+    import torch
+    from larynx_b200.hift import HiftVocoder, conv_flops
+    from larynx_b200.hift_weights import synthetic_source, write_source_asset, write_synthetic_hift_gguf
+    d = tempfile.mkdtemp(prefix="hift_bench_")
+    gp, sp = os.path.join(d, "hift.gguf"), os.path.join(d, "hift_source.bin")
+    write_synthetic_hift_gguf(gp, seed=0)
+    ri, bank = synthetic_source(0)
+    write_source_asset(sp, ri, bank)
+    del bank
+    v = HiftVocoder(dev.index or 0)
+    ok = v.load(gp) and v.load_source(sp)
+    for p in (gp, sp):
+        os.remove(p)
+    os.rmdir(d)
+    if not ok:
+        return {"error": v.last_error}
+    s = torch.cuda.Stream(dev)
+    mel = torch.randn(80, T, device=dev, generator=torch.Generator(dev).manual_seed(5))
+    audio = torch.empty(T * 480, device=dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    for _ in range(3):
+        v.vocode_device(mel.data_ptr(), T, audio.data_ptr(), s.cuda_stream)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(iters):
+        v.vocode_device(mel.data_ptr(), T, audio.data_ptr(), s.cuda_stream)
+    e1.record(s)
+    s.synchronize()
+    ms = e0.elapsed_time(e1) / iters
+    v.close()
+    fl = conv_flops(T)
+    props = torch.cuda.get_device_properties(dev)
+    peak = props.multi_processor_count * 128 * 2 * 1.965e9 / 1e12
+    return {"T_frames": T, "audio_s": T * 480 / 24000, "ms": round(ms, 3),
+            "mel_frames_per_s": round(T / (ms * 1e-3), 1), "rtf": (ms * 1e-3) / (T * 480 / 24000),
+            "conv_tflops": round(fl / (ms * 1e-3) / 1e12, 2),
+            "fp32_peak_nominal_tflops": round(peak, 1), "frac_of_fp32_peak_nominal": round(fl / (ms * 1e-3) / 1e12 / peak, 3),
+            "finite": bool(torch.isfinite(audio).all().item()),
+            "about": "whole vocoder (f0 fp64, SineGen2, STFT, fp32 conv network, ISTFT) per call; "
+                     "conv_tflops = conv-network FLOPs / whole-call time"}
+
+
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
@@ -514,6 +563,8 @@ def run_ours(args):
         extra["cfg1_ops"] = bench_cfg1(dev, stream)
     if not args.no_cfg4:
         extra["cfg4_stream"] = bench_cfg4(dec, dev, stream)
+    if world == 1 and not args.no_hift:
+        extra["hift"] = bench_hift(dev)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -554,6 +605,7 @@ def main():
     ap.add_argument("--no-cfg2", action="store_true")
     ap.add_argument("--no-cfg1", action="store_true")
     ap.add_argument("--no-cfg4", action="store_true")
+    ap.add_argument("--no-hift", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
