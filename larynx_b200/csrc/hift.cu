@@ -29,16 +29,20 @@
 //                  normalisation, clamp)
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdint>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <memory>
 #include <string>
 #include <vector>
 
 #include "../../include/larynx_hift.h"
+#include "common.cuh"
 #include "gguf.h"
+#include "kernels.h"
 
 namespace lx {
 namespace hift {
@@ -519,12 +523,247 @@ __global__ void k_transpose(const float* __restrict__ in, int L, int C, int act,
 }
 
 // ---------------------------------------------------------------------------
+// Tensor-core conv with a 3-term bf16 split (tcgen05, 1 CTA per SM)
+// ---------------------------------------------------------------------------
+// fp32 products to ~2^-17 relative on the bf16 tensor cores: each operand is
+// split v = hi + lo (hi = bf16(v), lo = bf16(v - hi)) and
+//   D = A_hi B_hi + A_hi B_lo + A_lo B_hi      (A_lo B_lo ~ 2^-18 |AB| dropped)
+// with fp32 accumulation.  A = the activation rows (time) of one tap and 64
+// channels, B = that tap's [BN out x 64 in] weight slice.  Per 16-wide K step
+// two MMAs: A_hi x [B_hi; B_lo] (N = 2 BN, into accumulator columns
+// [0, 2BN): hh | hl) and A_lo x B_hi (N = BN, added into [0, BN)); the
+// epilogue sums the two halves.  The K loop runs over (tap, 64-channel slice):
+// the A boxes of tap t are the 128-row tiles shifted by t*dil - pad_left rows
+// (TMA rows outside the tensor read as zero: the causal padding).
+//   warp 0      TMA: A_hi, A_lo (128 x 64) and B_hi, B_lo (BN x 64, adjacent
+//               in shared memory) per stage
+//   warp 1      TMEM allocator; lane 0 issues the MMAs
+//   warps 2..5  epilogue: TMEM -> registers, hh+lh + hl + bias (+ residual),
+//               fp32 stores
+constexpr int TC_THREADS = 192;
+
+struct TcConvArgs {
+  int L_out, C_out, K_taps, dil, pad_left, n_cb;
+  const float* bias;  // [C_out]
+  const float* res;   // [L_out][C_out] or null (may alias out)
+  float* out;         // [L_out][C_out]
+  int* err;
+};
+
+template <int BN>
+__host__ __device__ constexpr int tc_stages() { return BN == 64 ? 4 : 3; }
+template <int BN>
+__host__ __device__ constexpr int tc_stage_bytes() { return 2 * 128 * 64 * 2 + 2 * BN * 64 * 2; }
+template <int BN>
+__host__ __device__ constexpr int tc_smem_bytes() { return 1024 + tc_stages<BN>() * tc_stage_bytes<BN>() + 256; }
+
+template <int BN>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    k_hconv_tc(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
+               const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmBl, TcConvArgs a) {
+  constexpr int STAGES = tc_stages<BN>();
+  constexpr int A_BYTES = 128 * 64 * 2;
+  constexpr int B_BYTES = BN * 64 * 2;
+  constexpr int STAGE_BYTES = tc_stage_bytes<BN>();
+  constexpr uint32_t ACC_COLS = 2 * BN;
+  constexpr uint32_t TMEM_COLS = 4 * BN;  // two accumulators
+  constexpr uint32_t IDESC_HH_HL = idesc_bf16_f32(128, 2 * BN);
+  constexpr uint32_t IDESC_LH = idesc_bf16_f32(128, BN);
+  static_assert(2 * BN <= 256 && TMEM_COLS <= 512, "accumulator layout");
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 4);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmAh);
+    tma_prefetch_desc(&tmAl);
+    tma_prefetch_desc(&tmBh);
+    tma_prefetch_desc(&tmBl);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int tiles_n = a.C_out / BN;
+  const int n_tiles = ((a.L_out + 127) / 128) * tiles_n;
+  const int num_kb = a.K_taps * a.n_cb;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
+        const int m0 = (tile / tiles_n) * 128, n0 = (tile % tiles_n) * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!(ok = mbar_wait(&empty[stage], phase ^ 1u, a.err, abort_flag, DEV_TIMEOUT_PRODUCER))) break;
+          const int t = kb / a.n_cb, c = kb - t * a.n_cb;
+          const int y = m0 + t * a.dil - a.pad_left;
+          uint8_t* st = smem + stage * STAGE_BYTES;
+          mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+          tma_load_2d(st, &tmAh, &full[stage], c * 64, y);
+          tma_load_2d(st + A_BYTES, &tmAl, &full[stage], c * 64, y);
+          tma_load_2d(st + 2 * A_BYTES, &tmBh, &full[stage], c * 64, t * a.C_out + n0);
+          tma_load_2d(st + 2 * A_BYTES + B_BYTES, &tmBl, &full[stage], c * 64, t * a.C_out + n0);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint64_t d0 = sdesc_sw128(smem_u32(smem));
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
+        if (!(ok = mbar_wait(&tempty[acc], acc_phase ^ 1u, a.err, abort_flag, DEV_TIMEOUT_MMA))) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc) * ACC_COLS;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!(ok = mbar_wait(&full[stage], phase, a.err, abort_flag, DEV_TIMEOUT_MMA))) break;
+          tc_fence_after();
+          const uint64_t dah = d0 + static_cast<uint64_t>((stage * STAGE_BYTES) >> 4);
+          const uint64_t dal = dah + static_cast<uint64_t>(A_BYTES >> 4);
+          const uint64_t dbh = dah + static_cast<uint64_t>((2 * A_BYTES) >> 4);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            umma_ss(d_tmem, dah + 2 * k, dbh + 2 * k, IDESC_HH_HL, (kb > 0 || k > 0) ? 1u : 0u);
+            umma_ss(d_tmem, dal + 2 * k, dbh + 2 * k, IDESC_LH, 1u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+    }
+  } else {
+    // epilogue warps 2..5 -> TMEM lane quarters 2, 3, 0, 1
+    const int q = warp & 3;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+      const int m0 = (tile / tiles_n) * 128, n0 = (tile % tiles_n) * BN;
+      const bool ok = mbar_wait(&tfull[acc], acc_phase, a.err, abort_flag, DEV_TIMEOUT_EPILOGUE);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      tc_fence_after();
+      const int row = m0 + q * 32 + lane;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc) * ACC_COLS;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        float u[16], v[16];
+        tmem_ld16(t_row + c0, u);
+        tmem_ld16(t_row + BN + c0, v);
+        tmem_ld_wait();
+        if (row < a.L_out) {
+          const int col = n0 + c0;
+          const size_t o = static_cast<size_t>(row) * a.C_out + col;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (a.res) r = *reinterpret_cast<const float4*>(a.res + o + 4 * j);
+            const float4 b = *reinterpret_cast<const float4*>(a.bias + col + 4 * j);
+            float4 w;
+            w.x = __fadd_rn(__fadd_rn(__fadd_rn(u[4 * j + 0], v[4 * j + 0]), b.x), r.x);
+            w.y = __fadd_rn(__fadd_rn(__fadd_rn(u[4 * j + 1], v[4 * j + 1]), b.y), r.y);
+            w.z = __fadd_rn(__fadd_rn(__fadd_rn(u[4 * j + 2], v[4 * j + 2]), b.z), r.z);
+            w.w = __fadd_rn(__fadd_rn(__fadd_rn(u[4 * j + 3], v[4 * j + 3]), b.w), r.w);
+            *reinterpret_cast<float4*>(a.out + o + 4 * j) = w;
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// act(in_up) split into bf16 hi / lo planes [L_in*up][C] (the A operands of
+// k_hconv_tc), 8 channels per thread.
+__global__ void k_split(const float* __restrict__ in, int L_in, int C, int up, int act, float slope,
+                        const float* __restrict__ alpha, const float* __restrict__ inv, bf16* __restrict__ hi,
+                        bf16* __restrict__ lo) {
+  const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int c8 = C / 8;
+  if (i >= static_cast<size_t>(L_in) * up * c8) return;
+  const int u = static_cast<int>(i / c8), c = static_cast<int>(i % c8) * 8;
+  const int src = up == 1 ? u : u / up;
+  const float4* p = reinterpret_cast<const float4*>(in + static_cast<size_t>(src) * C + c);
+  const float4 x0 = __ldg(p), x1 = __ldg(p + 1);
+  float v[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+  uint32_t h[4], l[4];
+#pragma unroll
+  for (int e = 0; e < 8; e += 2) {
+    const float a0 = act_apply(v[e], act, slope, alpha, inv, c + e);
+    const float a1 = act_apply(v[e + 1], act, slope, alpha, inv, c + e + 1);
+    const bf16 h0 = __float2bfloat16_rn(a0), h1 = __float2bfloat16_rn(a1);
+    const bf16 l0 = __float2bfloat16_rn(__fsub_rn(a0, __bfloat162float(h0)));
+    const bf16 l1 = __float2bfloat16_rn(__fsub_rn(a1, __bfloat162float(h1)));
+    h[e / 2] = static_cast<uint32_t>(__bfloat16_as_ushort(h0)) | (static_cast<uint32_t>(__bfloat16_as_ushort(h1)) << 16);
+    l[e / 2] = static_cast<uint32_t>(__bfloat16_as_ushort(l0)) | (static_cast<uint32_t>(__bfloat16_as_ushort(l1)) << 16);
+  }
+  const size_t o = static_cast<size_t>(u) * C + c;
+  *reinterpret_cast<uint4*>(hi + o) = make_uint4(h[0], h[1], h[2], h[3]);
+  *reinterpret_cast<uint4*>(lo + o) = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+// ---------------------------------------------------------------------------
 // Device model
 // ---------------------------------------------------------------------------
 struct ConvW {
   float* wt = nullptr;  // [K][C_in][C_out_pad]
   float* b = nullptr;   // [C_out_pad]
   int C_in = 0, C_out = 0, C_out_pad = 0, K = 0;
+  // tensor-core form (C_in % 64 == 0, C_out % 64 == 0): bf16 hi / lo planes
+  // of W as [K][C_out][C_in] and their tensor maps for BN = 64 / 128
+  bf16* whi = nullptr;
+  bf16* wlo = nullptr;
+  bool tc = false;
+  CUtensorMap tmh[2], tml[2];
 };
 struct SnakeW {
   float* alpha = nullptr;
@@ -554,6 +793,8 @@ struct Work {
   float *s = nullptr, *stft = nullptr, *post = nullptr, *vw = nullptr, *audio = nullptr;
   float* act[8] = {};  // X, F, S1, S2, R0, R1, R2, T1
   float *sine_wavs = nullptr, *mag = nullptr, *pha = nullptr, *raw = nullptr, *stage = nullptr;
+  bf16 *ahi = nullptr, *alo = nullptr;  // split A operands of the tensor-core convs
+  int* err = nullptr;
 };
 
 }  // namespace hift
@@ -613,6 +854,13 @@ int read_t(lx_hift* h, GgufFile& g, const std::string& name, std::vector<int64_t
   return LX_OK;
 }
 
+// float -> bf16 bits, round to nearest even (finite inputs)
+uint16_t bf16_bits(float f) {
+  uint32_t u;
+  std::memcpy(&u, &f, 4);
+  return static_cast<uint16_t>((u + (((u >> 16) & 1u) + 0x7FFFu)) >> 16);
+}
+
 // Conv weight W[oc][ic][k] (PyTorch) -> wt[k][ic][oc], oc padded to a
 // multiple of 64 with zeros.
 int load_conv(lx_hift* h, GgufFile& g, const std::string& name, int C_out, int C_in, int K, ConvW* out) {
@@ -631,7 +879,33 @@ int load_conv(lx_hift* h, GgufFile& g, const std::string& name, int C_out, int C
   out->C_out_pad = pad;
   out->K = K;
   if (int rc = dupload(h, &out->wt, wt.data(), wt.size())) return rc;
-  return dupload(h, &out->b, bp.data(), bp.size());
+  if (int rc = dupload(h, &out->b, bp.data(), bp.size())) return rc;
+  if (C_in % 64 == 0 && C_out % 64 == 0) {
+    // hi = bf16(w), lo = bf16(w - hi), tap-major rows [k][oc] of C_in
+    std::vector<uint16_t> hb(static_cast<size_t>(K) * C_out * C_in), lb(hb.size());
+    for (int oc = 0; oc < C_out; ++oc)
+      for (int ic = 0; ic < C_in; ++ic)
+        for (int k = 0; k < K; ++k) {
+          const float v = w[(static_cast<size_t>(oc) * C_in + ic) * K + k];
+          const size_t o = (static_cast<size_t>(k) * C_out + oc) * C_in + ic;
+          hb[o] = bf16_bits(v);
+          const uint32_t bits = static_cast<uint32_t>(hb[o]) << 16;
+          float hv;
+          std::memcpy(&hv, &bits, 4);
+          lb[o] = bf16_bits(v - hv);
+        }
+    if (int rc = dupload(h, reinterpret_cast<uint16_t**>(&out->whi), hb.data(), hb.size())) return rc;
+    if (int rc = dupload(h, reinterpret_cast<uint16_t**>(&out->wlo), lb.data(), lb.size())) return rc;
+    const uint64_t rows = static_cast<uint64_t>(K) * C_out;
+    bool ok = tmap_bf16(&out->tmh[0], out->whi, rows, C_in, C_in, 64, 64) &&
+              tmap_bf16(&out->tml[0], out->wlo, rows, C_in, C_in, 64, 64);
+    if (ok && C_out % 128 == 0)
+      ok = tmap_bf16(&out->tmh[1], out->whi, rows, C_in, C_in, 128, 64) &&
+           tmap_bf16(&out->tml[1], out->wlo, rows, C_in, C_in, 128, 64);
+    if (!ok) return h->fail(LX_ERR_CUDA, "hift: tensor map of " + name);
+    out->tc = true;
+  }
+  return LX_OK;
 }
 
 int load_snake(lx_hift* h, GgufFile& g, const std::string& name, int C, SnakeW* out) {
@@ -710,7 +984,8 @@ void free_work(Work& w) {
                    reinterpret_cast<void**>(&w.s),     reinterpret_cast<void**>(&w.stft), reinterpret_cast<void**>(&w.post),
                    reinterpret_cast<void**>(&w.vw),    reinterpret_cast<void**>(&w.audio),
                    reinterpret_cast<void**>(&w.sine_wavs), reinterpret_cast<void**>(&w.mag),
-                   reinterpret_cast<void**>(&w.pha),   reinterpret_cast<void**>(&w.raw), reinterpret_cast<void**>(&w.stage)};
+                   reinterpret_cast<void**>(&w.pha),   reinterpret_cast<void**>(&w.raw), reinterpret_cast<void**>(&w.stage),
+                   reinterpret_cast<void**>(&w.ahi),   reinterpret_cast<void**>(&w.alo), reinterpret_cast<void**>(&w.err)};
   for (void** p : ptrs) wfree(*p);
   for (float*& p : w.act) {
     void* v = p;
@@ -722,6 +997,8 @@ void free_work(Work& w) {
 }
 
 size_t act_floats(int T) { return static_cast<size_t>(7680) * T + 64; }
+// largest tensor-core A operand: the x3 upsampled 128-channel input of ups.2
+size_t split_elems(int T) { return static_cast<size_t>(15360) * T + 64; }
 
 int ensure_work(lx_hift* h, int T, bool dbg) {
   Work& w = h->ws;
@@ -738,7 +1015,8 @@ int ensure_work(lx_hift* h, int T, bool dbg) {
             A(&w.y1, static_cast<size_t>(BASE_CH) * nT) && A(&w.mel, static_cast<size_t>(IN_CH) * nT) &&
             A(&w.melT, static_cast<size_t>(IN_CH) * nT) && A(&w.f0, nT) && A(&w.cums, static_cast<size_t>(HARM) * nT) &&
             A(&w.bank, L_S * HARM) && A(&w.rand, HARM) && A(&w.s, L_S) && A(&w.stft, N * OUT_CH) &&
-            A(&w.post, N * OUT_CH) && A(&w.vw, N * N_FFT) && A(&w.audio, L_S);
+            A(&w.post, N * OUT_CH) && A(&w.vw, N * N_FFT) && A(&w.audio, L_S) && A(&w.ahi, split_elems(nT)) &&
+            A(&w.alo, split_elems(nT)) && A(&w.err, 1);
   for (int i = 0; ok && i < 8; ++i) ok = A(&w.act[i], act_floats(nT));
   if (ok && nd)
     ok = A(&w.sine_wavs, L_S * HARM) && A(&w.mag, N * N_BINS) && A(&w.pha, N * N_BINS) && A(&w.raw, L_S) &&
@@ -765,8 +1043,51 @@ int num_sms_hift() {
   return n;
 }
 
-void hconv(cudaStream_t s, const float* in, int L_in, int C_in, int up, const ConvW& w, int dil, int pad_left,
-           int act, float slope, const SnakeW* sn, const float* res, float* out, int L_out) {
+// LX_HIFT_TC=0 keeps every conv on the fp32 CUDA-core kernel (A/B switch);
+// by default the convs with 64-multiple channel counts use k_hconv_tc.
+bool use_tc() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = std::getenv("LX_HIFT_TC");
+    v = (e && std::strcmp(e, "0") == 0) ? 0 : 1;
+  }
+  return v == 1;
+}
+
+// One conv of the network (see ConvArgs for the semantics).  Returns false
+// when a tensor map cannot be encoded.
+bool hconv(cudaStream_t s, const Work& ws, const float* in, int L_in, int C_in, int up, const ConvW& w, int dil,
+           int pad_left, int act, float slope, const SnakeW* sn, const float* res, float* out, int L_out) {
+  const int sms = num_sms_hift();
+  if (use_tc() && w.tc && C_in % 64 == 0) {
+    const size_t rows = static_cast<size_t>(L_in) * up;
+    const size_t n8 = rows * C_in / 8;
+    k_split<<<nblk(n8, 256), 256, 0, s>>>(in, L_in, C_in, up, act, slope, sn ? sn->alpha : nullptr,
+                                          sn ? sn->inv : nullptr, ws.ahi, ws.alo);
+    CUtensorMap ah, al;
+    if (!tmap_bf16(&ah, ws.ahi, rows, C_in, C_in, 128, 64) || !tmap_bf16(&al, ws.alo, rows, C_in, C_in, 128, 64))
+      return false;
+    TcConvArgs ta;
+    ta.L_out = L_out;
+    ta.C_out = w.C_out;
+    ta.K_taps = w.K;
+    ta.dil = dil;
+    ta.pad_left = pad_left;
+    ta.n_cb = C_in / 64;
+    ta.bias = w.b;
+    ta.res = res;
+    ta.out = out;
+    ta.err = ws.err;
+    const int tiles_m = static_cast<int>(nblk(static_cast<size_t>(L_out), 128));
+    if (w.C_out % 128 == 0 && tiles_m * (w.C_out / 128) >= sms) {
+      const int tiles = tiles_m * (w.C_out / 128);
+      k_hconv_tc<128><<<std::min(tiles, sms), TC_THREADS, tc_smem_bytes<128>(), s>>>(ah, al, w.tmh[1], w.tml[1], ta);
+    } else {
+      const int tiles = tiles_m * (w.C_out / 64);
+      k_hconv_tc<64><<<std::min(tiles, sms), TC_THREADS, tc_smem_bytes<64>(), s>>>(ah, al, w.tmh[0], w.tml[0], ta);
+    }
+    return true;
+  }
   ConvArgs a;
   a.in = in;
   a.L_in = L_in;
@@ -787,7 +1108,7 @@ void hconv(cudaStream_t s, const float* in, int L_in, int C_in, int up, const Co
   a.out = out;
   a.L_out = L_out;
   // the largest tile that still gives two waves of CTAs, else the smallest
-  const size_t waves2 = 2 * static_cast<size_t>(num_sms_hift());
+  const size_t waves2 = 2 * static_cast<size_t>(sms);
   const size_t g128 = nblk(static_cast<size_t>(L_out), 128), g64 = nblk(static_cast<size_t>(L_out), 64);
   if (w.C_out_pad % 128 == 0 && g128 * (w.C_out_pad / 128) >= waves2)
     k_hconv<128, 128><<<dim3(g128, w.C_out_pad / 128), HC_THREADS, 0, s>>>(a);
@@ -795,16 +1116,18 @@ void hconv(cudaStream_t s, const float* in, int L_in, int C_in, int up, const Co
     k_hconv<128, 64><<<dim3(g128, w.C_out_pad / 64), HC_THREADS, 0, s>>>(a);
   else
     k_hconv<64, 64><<<dim3(g64, w.C_out_pad / 64), HC_THREADS, 0, s>>>(a);
+  return true;
 }
 
 // resblock (hift.cpp:25-40): R = x after 3 x (snake1 -> conv1(d_j) -> snake2 -> conv2 + residual)
-void resblock(cudaStream_t s, const ResW& w, int k, const float* X, float* R, float* T1, int C, int L) {
+bool resblock(cudaStream_t s, const Work& ws, const ResW& w, int k, const float* X, float* R, float* T1, int C, int L) {
   for (int j = 0; j < 3; ++j) {
     const int d = RESBLOCK_DILATIONS[j];
     const float* src = j == 0 ? X : R;
-    hconv(s, src, L, C, 1, w.c1[j], d, d * (k - 1), ACT_SNAKE, 0.f, &w.a1[j], nullptr, T1, L);
-    hconv(s, T1, L, C, 1, w.c2[j], 1, k - 1, ACT_SNAKE, 0.f, &w.a2[j], src, R, L);
+    if (!hconv(s, ws, src, L, C, 1, w.c1[j], d, d * (k - 1), ACT_SNAKE, 0.f, &w.a1[j], nullptr, T1, L)) return false;
+    if (!hconv(s, ws, T1, L, C, 1, w.c2[j], 1, k - 1, ACT_SNAKE, 0.f, &w.a2[j], src, R, L)) return false;
   }
+  return true;
 }
 
 // Debug capture of a time-major device tensor into the caller's [C][L] buffer.
@@ -854,7 +1177,9 @@ int forward(lx_hift* h, const float* mel_dev, int T, const float* rand, const fl
   float *X = w.act[0], *F = w.act[1], *S1 = w.act[2], *S2 = w.act[3], *T1 = w.act[7];
   float* R[3] = {w.act[4], w.act[5], w.act[6]};
   // conv_pre: CausalConv1d(80 -> 512, k=5, right pad 4)
-  hconv(s, w.melT, T, IN_CH, 1, m.conv_pre, 1, 0, ACT_NONE, 0.f, nullptr, nullptr, X, T);
+  auto bad_map = [h]() { return h->fail(LX_ERR_CUDA, "hift: tensor map encoding failed"); };
+  HCK(cudaMemsetAsync(w.err, 0, sizeof(int), s));
+  if (!hconv(s, w, w.melT, T, IN_CH, 1, m.conv_pre, 1, 0, ACT_NONE, 0.f, nullptr, nullptr, X, T)) return bad_map();
   if (dbg)
     if (int rc = capture(h, dbg->conv_pre, X, T, BASE_CH)) return rc;
   int L_prev = T, C_prev = BASE_CH;
@@ -864,8 +1189,9 @@ int forward(lx_hift* h, const float* mel_dev, int T, const float* rand, const fl
       if (int rc = capture(h, dbg->ups_lrelu[i], X, L_prev, C_prev, ACT_LRELU, LRELU_SLOPE)) return rc;
     // CausalConv1dUpsample: leaky_relu -> nearest x rate -> left pad k-1 -> conv
     float* U = i == 2 ? F + C : F;
-    hconv(s, X, L_prev, C_prev, UPSAMPLE_RATES[i], m.ups[i], 1, UPSAMPLE_KERNELS[i] - 1, ACT_LRELU, LRELU_SLOPE,
-          nullptr, nullptr, U, L);
+    if (!hconv(s, w, X, L_prev, C_prev, UPSAMPLE_RATES[i], m.ups[i], 1, UPSAMPLE_KERNELS[i] - 1, ACT_LRELU,
+               LRELU_SLOPE, nullptr, nullptr, U, L))
+      return bad_map();
     if (dbg)
       if (int rc = capture(h, dbg->ups[i], U, L, C)) return rc;
     int Lf = L;
@@ -882,7 +1208,7 @@ int forward(lx_hift* h, const float* mel_dev, int T, const float* rand, const fl
         w.stft, N, OUT_CH, sd.wt, sd.b, C, sd.C_out_pad, sd.K, st, st == 1 ? 0 : st - 1, S1, Lf);
     if (dbg)
       if (int rc = capture(h, dbg->source_downs[i], S1, Lf, C)) return rc;
-    resblock(s, m.src_rb[i], SRC_RB_KERNELS[i], S1, S2, T1, C, Lf);
+    if (!resblock(s, w, m.src_rb[i], SRC_RB_KERNELS[i], S1, S2, T1, C, Lf)) return bad_map();
     if (dbg)
       if (int rc = capture(h, dbg->source_resblocks[i], S2, Lf, C)) return rc;
     const size_t n4 = static_cast<size_t>(Lf) * C / 4;
@@ -890,7 +1216,7 @@ int forward(lx_hift* h, const float* mel_dev, int T, const float* rand, const fl
     if (dbg)
       if (int rc = capture(h, dbg->fusion[i], F, Lf, C)) return rc;
     for (int j = 0; j < 3; ++j) {
-      resblock(s, m.rb[3 * i + j], RESBLOCK_KERNELS[j], F, R[j], T1, C, Lf);
+      if (!resblock(s, w, m.rb[3 * i + j], RESBLOCK_KERNELS[j], F, R[j], T1, C, Lf)) return bad_map();
       if (dbg)
         if (int rc = capture(h, dbg->resblocks[3 * i + j], R[j], Lf, C)) return rc;
     }
@@ -903,7 +1229,7 @@ int forward(lx_hift* h, const float* mel_dev, int T, const float* rand, const fl
   // final leaky_relu (slope 0.01) -> conv_post (k=7, left pad 6)
   if (dbg)
     if (int rc = capture(h, dbg->final_lrelu, X, N, 64, ACT_LRELU, 0.01f)) return rc;
-  hconv(s, X, N, 64, 1, m.conv_post, 1, 6, ACT_LRELU, 0.01f, nullptr, nullptr, w.post, N);
+  if (!hconv(s, w, X, N, 64, 1, m.conv_post, 1, 6, ACT_LRELU, 0.01f, nullptr, nullptr, w.post, N)) return bad_map();
   if (dbg)
     if (int rc = capture(h, dbg->conv_post, w.post, N, OUT_CH)) return rc;
   k_istft_frames<<<nblk(N, 128), 128, 0, s>>>(w.post, N, w.vw, dbg ? w.mag : nullptr, dbg ? w.pha : nullptr);
@@ -956,6 +1282,11 @@ extern "C" int lx_hift_create(int device, lx_hift** out) {
   h->device = device;
   if (cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking) != cudaSuccess) return LX_ERR_CUDA;
   if (lx::hift::upload_dft(h.get()) != LX_OK) return LX_ERR_CUDA;
+  if (cudaFuncSetAttribute(lx::hift::k_hconv_tc<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           lx::hift::tc_smem_bytes<64>()) != cudaSuccess ||
+      cudaFuncSetAttribute(lx::hift::k_hconv_tc<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           lx::hift::tc_smem_bytes<128>()) != cudaSuccess)
+    return LX_ERR_CUDA;
   *out = h.release();
   return LX_OK;
 }
@@ -1057,8 +1388,12 @@ extern "C" int lx_hift_vocode(lx_hift* h, const float* mel, int T, const float* 
   }
   if (int rc = lx::hift::forward(h, w.mel, T, rand, bank, s, debug)) return rc;
   VCK(cudaMemcpyAsync(audio, w.audio, L_S * sizeof(float), cudaMemcpyDeviceToHost, s));
+  int dev_err = 0;
+  VCK(cudaMemcpyAsync(&dev_err, w.err, sizeof(int), cudaMemcpyDeviceToHost, s));
   VCK(cudaStreamSynchronize(s));
 #undef VCK
+  if (dev_err) return h->fail(LX_ERR_TIMEOUT, "hift: a device-side wait exceeded its bound (code " +
+                                                   std::to_string(dev_err) + ")");
   return LX_OK;
 }
 
