@@ -80,23 +80,58 @@ inline int stage_channels(int i) { return BASE_CH >> (i + 1); }
 // f0 predictor (float64, channel-major [C][T])
 // ---------------------------------------------------------------------------
 // out[oc][t] = b[oc] + sum_ic sum_k W[oc][ic][k] x[ic][t + k - pad_left]
-// (source.cpp:18-35), then ELU when `elu`.  Block: 128 consecutive t of one oc.
-__global__ void k_f0_conv(const double* __restrict__ x, int L, int IC, const double* __restrict__ W,
-                          const double* __restrict__ b, int K, int pad_left, int elu, double* __restrict__ out) {
-  const int oc = blockIdx.y;
-  const int t = blockIdx.x * blockDim.x + threadIdx.x;
-  if (t >= L) return;
-  double acc = b[oc];
-  const double* wr = W + static_cast<size_t>(oc) * IC * K;
-  for (int ic = 0; ic < IC; ++ic) {
-    const double* xr = x + static_cast<size_t>(ic) * L;
-    for (int k = 0; k < K; ++k) {
-      const int src = t + k - pad_left;
-      if (src >= 0 && src < L) acc = __dadd_rn(acc, __dmul_rn(wr[ic * K + k], xr[src]));
+// (source.cpp:18-35), then ELU when `elu`.  Each output keeps the
+// reference's order (bias, ic ascending, k ascending, out-of-range taps
+// skipped) with separately rounded products and sums.  Block: 64 t x 32 oc,
+// thread = one t and 8 oc; 8-channel slices of x and W staged in shared
+// memory so each x value feeds 8 outputs and each W value 64.
+constexpr int F0_BT = 64, F0_BO = 32, F0_BC = 8, F0_KMAX = 4;
+
+__global__ void __launch_bounds__(256) k_f0_conv(const double* __restrict__ x, int L, int IC,
+                                                 const double* __restrict__ W, const double* __restrict__ b, int K,
+                                                 int pad_left, int elu, double* __restrict__ out) {
+  __shared__ double xs[F0_BC][F0_BT + F0_KMAX - 1];
+  __shared__ double ws[F0_BC][F0_KMAX][F0_BO];
+  const int tid = threadIdx.x, tx = tid & 63, ty = tid >> 6;  // ty: 8-oc group 0..3
+  const int t0 = blockIdx.x * F0_BT, oc0 = blockIdx.y * F0_BO;
+  const int t = t0 + tx;
+  double acc[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) acc[j] = b[oc0 + ty * 8 + j];
+  bool valid[F0_KMAX];
+#pragma unroll
+  for (int k = 0; k < F0_KMAX; ++k) valid[k] = k < K && t + k - pad_left >= 0 && t + k - pad_left < L;
+  const int WR = F0_BT + K - 1;
+  for (int ic0 = 0; ic0 < IC; ic0 += F0_BC) {
+    const int nc = min(F0_BC, IC - ic0);
+    for (int i = tid; i < F0_BC * WR; i += 256) {
+      const int c = i / WR, r = i - c * WR;
+      const int src = t0 + r - pad_left;
+      xs[c][r] = (c < nc && src >= 0 && src < L) ? x[static_cast<size_t>(ic0 + c) * L + src] : 0.0;
     }
+    for (int i = tid; i < F0_BC * K * F0_BO; i += 256) {
+      const int o = i % F0_BO, ck = i / F0_BO, c = ck / K, k = ck - c * K;
+      ws[c][k][o] = c < nc ? W[(static_cast<size_t>(oc0 + o) * IC + ic0 + c) * K + k] : 0.0;
+    }
+    __syncthreads();
+    for (int c = 0; c < nc; ++c) {
+#pragma unroll
+      for (int k = 0; k < F0_KMAX; ++k) {
+        if (!valid[k]) continue;
+        const double xv = xs[c][tx + k];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] = __dadd_rn(acc[j], __dmul_rn(ws[c][k][ty * 8 + j], xv));
+      }
+    }
+    __syncthreads();
   }
-  if (elu && acc <= 0.0) acc = exp(acc) - 1.0;
-  out[static_cast<size_t>(oc) * L + t] = acc;
+  if (t >= L) return;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    double v = acc[j];
+    if (elu && v <= 0.0) v = exp(v) - 1.0;
+    out[static_cast<size_t>(oc0 + ty * 8 + j) * L + t] = v;
+  }
 }
 
 // f0[t] = |b + sum_ic w[ic] y[ic][t]| (source.cpp:89-95), cast to float32;
@@ -130,22 +165,30 @@ __device__ __forceinline__ float rad_at(const float* f0, const float* rand_ini, 
   return r;
 }
 
-// Per harmonic: the linear x(1/480) downsample of rad (align_corners=False)
-// and its running sum over frames, serially in frame order (source.cpp:117-139).
-__global__ void k_sine_cumsum(const float* __restrict__ f0, const float* __restrict__ rand_ini, int T,
-                              float* __restrict__ cums) {
+// rad_down[i][h]: the linear x(1/480) downsample of rad, align_corners=False
+// (source.cpp:117-129), one thread per (frame, harmonic).
+__global__ void k_rad_down(const float* __restrict__ f0, const float* __restrict__ rand_ini, int T,
+                           float* __restrict__ rd) {
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= T * HARM) return;
+  const int i = idx / HARM, h = idx - i * HARM;
+  const int L_S = T * TOTAL_SCALE;
+  const float src = __fsub_rn(__fmul_rn(__fadd_rn(static_cast<float>(i), 0.5f), static_cast<float>(L_S / T)), 0.5f);
+  const int f = static_cast<int>(floorf(src));
+  const int c = min(f + 1, L_S - 1);
+  const float frac = __fsub_rn(src, static_cast<float>(f));
+  rd[idx] = __fadd_rn(__fmul_rn(rad_at(f0, rand_ini, f, h), __fsub_rn(1.0f, frac)),
+                      __fmul_rn(rad_at(f0, rand_ini, c, h), frac));
+}
+
+// Per harmonic the running sum over frames, serially in frame order
+// (source.cpp:131-139), in place.
+__global__ void k_sine_cumsum(float* __restrict__ cums, int T) {
   const int h = threadIdx.x;
   if (h >= HARM) return;
-  const int L_S = T * TOTAL_SCALE;
   float acc = 0.0f;
   for (int i = 0; i < T; ++i) {
-    const float src = __fsub_rn(__fmul_rn(__fadd_rn(static_cast<float>(i), 0.5f), static_cast<float>(L_S / T)), 0.5f);
-    const int f = static_cast<int>(floorf(src));
-    const int c = min(f + 1, L_S - 1);
-    const float frac = __fsub_rn(src, static_cast<float>(f));
-    const float v = __fadd_rn(__fmul_rn(rad_at(f0, rand_ini, f, h), __fsub_rn(1.0f, frac)),
-                              __fmul_rn(rad_at(f0, rand_ini, c, h), frac));
-    acc = __fadd_rn(acc, v);
+    acc = __fadd_rn(acc, cums[i * HARM + h]);
     cums[i * HARM + h] = acc;
   }
 }
@@ -459,22 +502,32 @@ __global__ void __launch_bounds__(HC_THREADS) k_hconv(ConvArgs a) {
 }
 
 // Direct conv for few input channels (the strided source downsampling of the
-// 18-channel STFT): one thread per output, oc fastest.
+// 18-channel STFT): one thread per (row, 4 output channels), C_out % 4 == 0.
 __global__ void k_conv_direct(const float* __restrict__ in, int L_in, int C_in, const float* __restrict__ wt,
                               const float* __restrict__ bias, int C_out, int C_out_pad, int K, int stride,
                               int pad_left, float* __restrict__ out, int L_out) {
+  const int c4 = C_out / 4;
   const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i >= static_cast<size_t>(L_out) * C_out) return;
-  const int t = static_cast<int>(i / C_out), oc = static_cast<int>(i % C_out);
-  float acc = 0.0f;
+  if (i >= static_cast<size_t>(L_out) * c4) return;
+  const int t = static_cast<int>(i / c4), oc = static_cast<int>(i % c4) * 4;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int k = 0; k < K; ++k) {
     const int src = t * stride + k - pad_left;
     if (src < 0 || src >= L_in) continue;
     const float* x = in + static_cast<size_t>(src) * C_in;
     const float* w = wt + static_cast<size_t>(k) * C_in * C_out_pad + oc;
-    for (int ic = 0; ic < C_in; ++ic) acc = fmaf(x[ic], w[static_cast<size_t>(ic) * C_out_pad], acc);
+    for (int ic = 0; ic < C_in; ++ic) {
+      const float xv = x[ic];
+      const float4 wv = __ldg(reinterpret_cast<const float4*>(w + static_cast<size_t>(ic) * C_out_pad));
+      acc.x = fmaf(xv, wv.x, acc.x);
+      acc.y = fmaf(xv, wv.y, acc.y);
+      acc.z = fmaf(xv, wv.z, acc.z);
+      acc.w = fmaf(xv, wv.w, acc.w);
+    }
   }
-  out[i] = __fadd_rn(acc, bias[oc]);
+  const float4 bv = *reinterpret_cast<const float4*>(bias + oc);
+  *reinterpret_cast<float4*>(out + static_cast<size_t>(t) * C_out + oc) =
+      make_float4(__fadd_rn(acc.x, bv.x), __fadd_rn(acc.y, bv.y), __fadd_rn(acc.z, bv.z), __fadd_rn(acc.w, bv.w));
 }
 
 __global__ void k_add(const float* __restrict__ a, const float* __restrict__ b, float* __restrict__ o, size_t n4) {
@@ -544,9 +597,10 @@ constexpr int TC_THREADS = 192;
 
 struct TcConvArgs {
   int L_out, C_out, K_taps, dil, pad_left, n_cb;
+  int ldo;            // real output channels (<= C_out, the 64-padded tile count): row stride of res / out
   const float* bias;  // [C_out]
-  const float* res;   // [L_out][C_out] or null (may alias out)
-  float* out;         // [L_out][C_out]
+  const float* res;   // [L_out][ldo] or null (may alias out)
+  float* out;         // [L_out][ldo]
   int* err;
 };
 
@@ -690,9 +744,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         tmem_ld16(t_row + c0, u);
         tmem_ld16(t_row + BN + c0, v);
         tmem_ld_wait();
-        if (row < a.L_out) {
-          const int col = n0 + c0;
-          const size_t o = static_cast<size_t>(row) * a.C_out + col;
+        const int col = n0 + c0;
+        if (row < a.L_out && (col + 16 > a.ldo || (a.ldo & 3))) {
+          // ragged last columns (conv_post's 18 outputs): scalar stores
+          const size_t o = static_cast<size_t>(row) * a.ldo + col;
+          for (int e = 0; e < 16 && col + e < a.ldo; ++e) {
+            float w = __fadd_rn(__fadd_rn(u[e], v[e]), a.bias[col + e]);
+            if (a.res) w = __fadd_rn(w, a.res[o + e]);
+            a.out[o + e] = w;
+          }
+        } else if (row < a.L_out) {
+          const size_t o = static_cast<size_t>(row) * a.ldo + col;
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -880,14 +942,15 @@ int load_conv(lx_hift* h, GgufFile& g, const std::string& name, int C_out, int C
   out->K = K;
   if (int rc = dupload(h, &out->wt, wt.data(), wt.size())) return rc;
   if (int rc = dupload(h, &out->b, bp.data(), bp.size())) return rc;
-  if (C_in % 64 == 0 && C_out % 64 == 0) {
-    // hi = bf16(w), lo = bf16(w - hi), tap-major rows [k][oc] of C_in
-    std::vector<uint16_t> hb(static_cast<size_t>(K) * C_out * C_in), lb(hb.size());
+  if (C_in % 64 == 0) {
+    // hi = bf16(w), lo = bf16(w - hi), tap-major rows [k][oc] of C_in, oc
+    // padded to `pad` with zero rows
+    std::vector<uint16_t> hb(static_cast<size_t>(K) * pad * C_in, 0), lb(hb.size(), 0);
     for (int oc = 0; oc < C_out; ++oc)
       for (int ic = 0; ic < C_in; ++ic)
         for (int k = 0; k < K; ++k) {
           const float v = w[(static_cast<size_t>(oc) * C_in + ic) * K + k];
-          const size_t o = (static_cast<size_t>(k) * C_out + oc) * C_in + ic;
+          const size_t o = (static_cast<size_t>(k) * pad + oc) * C_in + ic;
           hb[o] = bf16_bits(v);
           const uint32_t bits = static_cast<uint32_t>(hb[o]) << 16;
           float hv;
@@ -896,10 +959,10 @@ int load_conv(lx_hift* h, GgufFile& g, const std::string& name, int C_out, int C
         }
     if (int rc = dupload(h, reinterpret_cast<uint16_t**>(&out->whi), hb.data(), hb.size())) return rc;
     if (int rc = dupload(h, reinterpret_cast<uint16_t**>(&out->wlo), lb.data(), lb.size())) return rc;
-    const uint64_t rows = static_cast<uint64_t>(K) * C_out;
+    const uint64_t rows = static_cast<uint64_t>(K) * pad;
     bool ok = tmap_bf16(&out->tmh[0], out->whi, rows, C_in, C_in, 64, 64) &&
               tmap_bf16(&out->tml[0], out->wlo, rows, C_in, C_in, 64, 64);
-    if (ok && C_out % 128 == 0)
+    if (ok && pad % 128 == 0)
       ok = tmap_bf16(&out->tmh[1], out->whi, rows, C_in, C_in, 128, 64) &&
            tmap_bf16(&out->tml[1], out->wlo, rows, C_in, C_in, 128, 64);
     if (!ok) return h->fail(LX_ERR_CUDA, "hift: tensor map of " + name);
@@ -1069,7 +1132,8 @@ bool hconv(cudaStream_t s, const Work& ws, const float* in, int L_in, int C_in, 
       return false;
     TcConvArgs ta;
     ta.L_out = L_out;
-    ta.C_out = w.C_out;
+    ta.C_out = w.C_out_pad;
+    ta.ldo = w.C_out;
     ta.K_taps = w.K;
     ta.dil = dil;
     ta.pad_left = pad_left;
@@ -1079,11 +1143,11 @@ bool hconv(cudaStream_t s, const Work& ws, const float* in, int L_in, int C_in, 
     ta.out = out;
     ta.err = ws.err;
     const int tiles_m = static_cast<int>(nblk(static_cast<size_t>(L_out), 128));
-    if (w.C_out % 128 == 0 && tiles_m * (w.C_out / 128) >= sms) {
-      const int tiles = tiles_m * (w.C_out / 128);
+    if (w.C_out_pad % 128 == 0 && tiles_m * (w.C_out_pad / 128) >= sms) {
+      const int tiles = tiles_m * (w.C_out_pad / 128);
       k_hconv_tc<128><<<std::min(tiles, sms), TC_THREADS, tc_smem_bytes<128>(), s>>>(ah, al, w.tmh[1], w.tml[1], ta);
     } else {
-      const int tiles = tiles_m * (w.C_out / 64);
+      const int tiles = tiles_m * (w.C_out_pad / 64);
       k_hconv_tc<64><<<std::min(tiles, sms), TC_THREADS, tc_smem_bytes<64>(), s>>>(ah, al, w.tmh[0], w.tml[0], ta);
     }
     return true;
@@ -1157,15 +1221,17 @@ int forward(lx_hift* h, const float* mel_dev, int T, const float* rand, const fl
   const int L_S = T * TOTAL_SCALE, N = L_S / HOP + 1;
   // f0 predictor (float64)
   k_mel_prep<<<nblk(static_cast<size_t>(IN_CH) * T, 256), 256, 0, s>>>(mel_dev, T, w.mel_d, w.melT);
-  k_f0_conv<<<dim3(nblk(T, 128), BASE_CH), 128, 0, s>>>(w.mel_d, T, IN_CH, m.f0_w[0], m.f0_b[0], 4, 0, 1, w.y0);
+  const dim3 f0_grid(nblk(T, F0_BT), BASE_CH / F0_BO);
+  k_f0_conv<<<f0_grid, 256, 0, s>>>(w.mel_d, T, IN_CH, m.f0_w[0], m.f0_b[0], 4, 0, 1, w.y0);
   double *ya = w.y0, *yb = w.y1;
   for (int i = 1; i < 5; ++i) {
-    k_f0_conv<<<dim3(nblk(T, 128), BASE_CH), 128, 0, s>>>(ya, T, BASE_CH, m.f0_w[i], m.f0_b[i], 3, 2, 1, yb);
+    k_f0_conv<<<f0_grid, 256, 0, s>>>(ya, T, BASE_CH, m.f0_w[i], m.f0_b[i], 3, 2, 1, yb);
     std::swap(ya, yb);
   }
   k_f0_cls<<<nblk(T, 128), 128, 0, s>>>(ya, T, m.cls_w, m.cls_b, w.f0);
   // SineGen2 + m_source + STFT
-  k_sine_cumsum<<<1, 32, 0, s>>>(w.f0, rand, T, w.cums);
+  k_rad_down<<<nblk(static_cast<size_t>(T) * HARM, 256), 256, 0, s>>>(w.f0, rand, T, w.cums);
+  k_sine_cumsum<<<1, 32, 0, s>>>(w.cums, T);
   k_source<<<nblk(L_S, 256), 256, 0, s>>>(w.f0, w.cums, bank, m.msw, m.msb, T, w.s, dbg ? w.sine_wavs : nullptr);
   k_stft<<<nblk(N, 128), 128, 0, s>>>(w.s, L_S, w.stft);
   if (dbg) {
@@ -1204,7 +1270,7 @@ int forward(lx_hift* h, const float* mel_dev, int T, const float* rand, const fl
     // source branch: CausalConv1dDownSample (left pad stride-1), resblock
     const int st = SRC_DOWN_STRIDES[i];
     const ConvW& sd = m.src_down[i];
-    k_conv_direct<<<nblk(static_cast<size_t>(Lf) * C, 256), 256, 0, s>>>(
+    k_conv_direct<<<nblk(static_cast<size_t>(Lf) * C / 4, 256), 256, 0, s>>>(
         w.stft, N, OUT_CH, sd.wt, sd.b, C, sd.C_out_pad, sd.K, st, st == 1 ? 0 : st - 1, S1, Lf);
     if (dbg)
       if (int rc = capture(h, dbg->source_downs[i], S1, Lf, C)) return rc;
