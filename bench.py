@@ -608,9 +608,15 @@ def main():
     ap.add_argument("--no-cfg1", action="store_true")
     ap.add_argument("--no-cfg4", action="store_true")
     ap.add_argument("--no-hift", action="store_true")
+    ap.add_argument("--only-hift", action="store_true",
+                    help="time only the HiFT vocoder (one 20 s utterance) and print its JSON object")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
+    if args.only_hift:
+        import torch
+        print(json.dumps(bench_hift(torch.device("cuda", 0))))
+        return
     if args.impl == "reference":
         run_reference(args)
     else:

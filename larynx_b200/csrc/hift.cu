@@ -85,23 +85,24 @@ inline int stage_channels(int i) { return BASE_CH >> (i + 1); }
 // skipped) with separately rounded products and sums.  Block: 64 t x 32 oc,
 // thread = one t and 8 oc; 8-channel slices of x and W staged in shared
 // memory so each x value feeds 8 outputs and each W value 64.
-constexpr int F0_BT = 64, F0_BO = 32, F0_BC = 8, F0_KMAX = 4;
+constexpr int F0_BT = 64, F0_BO = 32, F0_BC = 8;
 
+template <int K>
 __global__ void __launch_bounds__(256) k_f0_conv(const double* __restrict__ x, int L, int IC,
-                                                 const double* __restrict__ W, const double* __restrict__ b, int K,
+                                                 const double* __restrict__ W, const double* __restrict__ b,
                                                  int pad_left, int elu, double* __restrict__ out) {
-  __shared__ double xs[F0_BC][F0_BT + F0_KMAX - 1];
-  __shared__ double ws[F0_BC][F0_KMAX][F0_BO];
+  constexpr int WR = F0_BT + K - 1;
+  __shared__ double xs[F0_BC][WR];
+  __shared__ __align__(16) double ws[F0_BC][K][F0_BO];
   const int tid = threadIdx.x, tx = tid & 63, ty = tid >> 6;  // ty: 8-oc group 0..3
   const int t0 = blockIdx.x * F0_BT, oc0 = blockIdx.y * F0_BO;
   const int t = t0 + tx;
   double acc[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) acc[j] = b[oc0 + ty * 8 + j];
-  bool valid[F0_KMAX];
+  bool valid[K];
 #pragma unroll
-  for (int k = 0; k < F0_KMAX; ++k) valid[k] = k < K && t + k - pad_left >= 0 && t + k - pad_left < L;
-  const int WR = F0_BT + K - 1;
+  for (int k = 0; k < K; ++k) valid[k] = t + k - pad_left >= 0 && t + k - pad_left < L;
   for (int ic0 = 0; ic0 < IC; ic0 += F0_BC) {
     const int nc = min(F0_BC, IC - ic0);
     for (int i = tid; i < F0_BC * WR; i += 256) {
@@ -109,18 +110,24 @@ __global__ void __launch_bounds__(256) k_f0_conv(const double* __restrict__ x, i
       const int src = t0 + r - pad_left;
       xs[c][r] = (c < nc && src >= 0 && src < L) ? x[static_cast<size_t>(ic0 + c) * L + src] : 0.0;
     }
-    for (int i = tid; i < F0_BC * K * F0_BO; i += 256) {
-      const int o = i % F0_BO, ck = i / F0_BO, c = ck / K, k = ck - c * K;
-      ws[c][k][o] = c < nc ? W[(static_cast<size_t>(oc0 + o) * IC + ic0 + c) * K + k] : 0.0;
+    // W[oc][ic0 .. ic0+7][0 .. K-1] is contiguous per oc: 8K doubles
+    for (int i = tid; i < F0_BO * F0_BC * K; i += 256) {
+      const int o = i / (F0_BC * K), e = i - o * (F0_BC * K), c = e / K, k = e - c * K;
+      ws[c][k][o] = c < nc ? W[(static_cast<size_t>(oc0 + o) * IC + ic0) * K + e] : 0.0;
     }
     __syncthreads();
     for (int c = 0; c < nc; ++c) {
 #pragma unroll
-      for (int k = 0; k < F0_KMAX; ++k) {
+      for (int k = 0; k < K; ++k) {
         if (!valid[k]) continue;
         const double xv = xs[c][tx + k];
+        const double2* wp = reinterpret_cast<const double2*>(&ws[c][k][ty * 8]);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[j] = __dadd_rn(acc[j], __dmul_rn(ws[c][k][ty * 8 + j], xv));
+        for (int j = 0; j < 4; ++j) {
+          const double2 wv = wp[j];
+          acc[2 * j] = __dadd_rn(acc[2 * j], __dmul_rn(wv.x, xv));
+          acc[2 * j + 1] = __dadd_rn(acc[2 * j + 1], __dmul_rn(wv.y, xv));
+        }
       }
     }
     __syncthreads();
@@ -591,18 +598,39 @@ __global__ void k_transpose(const float* __restrict__ in, int L, int C, int act,
 //   warp 0      TMA: A_hi, A_lo (128 x 64) and B_hi, B_lo (BN x 64, adjacent
 //               in shared memory) per stage
 //   warp 1      TMEM allocator; lane 0 issues the MMAs
-//   warps 2..5  epilogue: TMEM -> registers, hh+lh + hl + bias (+ residual),
-//               fp32 stores
-constexpr int TC_THREADS = 192;
+//   warps 2..17 epilogue, four warps per TMEM lane quarter (each a quarter
+//               of the columns): TMEM -> registers, hh+lh + hl + bias
+//               (+ residual), fp32 stores and / or the next conv's split
+//               operands (the Snake of the next conv makes this the heavy
+//               part for the short convs, hence the many warps)
+constexpr int TC_THREADS = 576;  // warp 0 TMA, warp 1 MMA, warps 2..17 epilogue
 
 struct TcConvArgs {
   int L_out, C_out, K_taps, dil, pad_left, n_cb;
   int ldo;            // real output channels (<= C_out, the 64-padded tile count): row stride of res / out
   const float* bias;  // [C_out]
   const float* res;   // [L_out][ldo] or null (may alias out)
-  float* out;         // [L_out][ldo]
+  float* out;         // [L_out][ldo], or null when only the split output is needed
   int* err;
+  // optional: the next conv's A operands, split(act(out)) as bf16 hi / lo
+  // [L_out][ldo] (ldo % 16 == 0)
+  bf16* nhi;
+  bf16* nlo;
+  int nact;
+  float nslope;
+  const float* nalpha;
+  const float* ninv;
 };
+
+// (hi pair, lo pair) of two values: hi = bf16(a), lo = bf16(a - hi)
+__device__ __forceinline__ uint2 split_pair(float a0, float a1) {
+  const bf16 h0 = __float2bfloat16_rn(a0), h1 = __float2bfloat16_rn(a1);
+  const bf16 l0 = __float2bfloat16_rn(__fsub_rn(a0, __bfloat162float(h0)));
+  const bf16 l1 = __float2bfloat16_rn(__fsub_rn(a1, __bfloat162float(h1)));
+  return make_uint2(
+      static_cast<uint32_t>(__bfloat16_as_ushort(h0)) | (static_cast<uint32_t>(__bfloat16_as_ushort(h1)) << 16),
+      static_cast<uint32_t>(__bfloat16_as_ushort(l0)) | (static_cast<uint32_t>(__bfloat16_as_ushort(l1)) << 16));
+}
 
 template <int BN>
 __host__ __device__ constexpr int tc_stages() { return BN == 64 ? 4 : 3; }
@@ -643,7 +671,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], 4);
+      mbar_init(&tempty[i], 16);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -727,8 +755,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       }
     }
   } else {
-    // epilogue warps 2..5 -> TMEM lane quarters 2, 3, 0, 1
+    // epilogue warps 2..17 -> TMEM lane quarter warp % 4; warps 2..5 take
+    // columns [0, BN/4), 6..9 [BN/4, BN/2), ...
     const int q = warp & 3;
+    const int cbeg = ((warp - 2) >> 2) * (BN / 4);
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
@@ -739,7 +769,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const int row = m0 + q * 32 + lane;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc) * ACC_COLS;
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 16) {
+      for (int c0 = cbeg; c0 < cbeg + BN / 4; c0 += 16) {
         float u[16], v[16];
         tmem_ld16(t_row + c0, u);
         tmem_ld16(t_row + BN + c0, v);
@@ -748,24 +778,42 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         if (row < a.L_out && (col + 16 > a.ldo || (a.ldo & 3))) {
           // ragged last columns (conv_post's 18 outputs): scalar stores
           const size_t o = static_cast<size_t>(row) * a.ldo + col;
-          for (int e = 0; e < 16 && col + e < a.ldo; ++e) {
-            float w = __fadd_rn(__fadd_rn(u[e], v[e]), a.bias[col + e]);
-            if (a.res) w = __fadd_rn(w, a.res[o + e]);
-            a.out[o + e] = w;
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            if (col + e < a.ldo) {
+              float w = __fadd_rn(__fadd_rn(u[e], v[e]), a.bias[col + e]);
+              if (a.res) w = __fadd_rn(w, a.res[o + e]);
+              a.out[o + e] = w;
+            }
           }
         } else if (row < a.L_out) {
           const size_t o = static_cast<size_t>(row) * a.ldo + col;
+          float w[16];
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
             if (a.res) r = *reinterpret_cast<const float4*>(a.res + o + 4 * j);
             const float4 b = *reinterpret_cast<const float4*>(a.bias + col + 4 * j);
-            float4 w;
-            w.x = __fadd_rn(__fadd_rn(__fadd_rn(u[4 * j + 0], v[4 * j + 0]), b.x), r.x);
-            w.y = __fadd_rn(__fadd_rn(__fadd_rn(u[4 * j + 1], v[4 * j + 1]), b.y), r.y);
-            w.z = __fadd_rn(__fadd_rn(__fadd_rn(u[4 * j + 2], v[4 * j + 2]), b.z), r.z);
-            w.w = __fadd_rn(__fadd_rn(__fadd_rn(u[4 * j + 3], v[4 * j + 3]), b.w), r.w);
-            *reinterpret_cast<float4*>(a.out + o + 4 * j) = w;
+            w[4 * j + 0] = __fadd_rn(__fadd_rn(__fadd_rn(u[4 * j + 0], v[4 * j + 0]), b.x), r.x);
+            w[4 * j + 1] = __fadd_rn(__fadd_rn(__fadd_rn(u[4 * j + 1], v[4 * j + 1]), b.y), r.y);
+            w[4 * j + 2] = __fadd_rn(__fadd_rn(__fadd_rn(u[4 * j + 2], v[4 * j + 2]), b.z), r.z);
+            w[4 * j + 3] = __fadd_rn(__fadd_rn(__fadd_rn(u[4 * j + 3], v[4 * j + 3]), b.w), r.w);
+            if (a.out)
+              *reinterpret_cast<float4*>(a.out + o + 4 * j) =
+                  make_float4(w[4 * j + 0], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+          }
+          if (a.nhi) {
+            uint32_t hi[8], lo[8];
+#pragma unroll
+            for (int e = 0; e < 16; e += 2) {
+              const float a0 = act_apply(w[e], a.nact, a.nslope, a.nalpha, a.ninv, col + e);
+              const float a1 = act_apply(w[e + 1], a.nact, a.nslope, a.nalpha, a.ninv, col + e + 1);
+              const uint2 p = split_pair(a0, a1);
+              hi[e / 2] = p.x;
+              lo[e / 2] = p.y;
+            }
+            st_global_v8(a.nhi + o, hi[0], hi[1], hi[2], hi[3], hi[4], hi[5], hi[6], hi[7]);
+            st_global_v8(a.nlo + o, lo[0], lo[1], lo[2], lo[3], lo[4], lo[5], lo[6], lo[7]);
           }
         }
       }
@@ -802,11 +850,9 @@ __global__ void k_split(const float* __restrict__ in, int L_in, int C, int up, i
   for (int e = 0; e < 8; e += 2) {
     const float a0 = act_apply(v[e], act, slope, alpha, inv, c + e);
     const float a1 = act_apply(v[e + 1], act, slope, alpha, inv, c + e + 1);
-    const bf16 h0 = __float2bfloat16_rn(a0), h1 = __float2bfloat16_rn(a1);
-    const bf16 l0 = __float2bfloat16_rn(__fsub_rn(a0, __bfloat162float(h0)));
-    const bf16 l1 = __float2bfloat16_rn(__fsub_rn(a1, __bfloat162float(h1)));
-    h[e / 2] = static_cast<uint32_t>(__bfloat16_as_ushort(h0)) | (static_cast<uint32_t>(__bfloat16_as_ushort(h1)) << 16);
-    l[e / 2] = static_cast<uint32_t>(__bfloat16_as_ushort(l0)) | (static_cast<uint32_t>(__bfloat16_as_ushort(l1)) << 16);
+    const uint2 p = split_pair(a0, a1);
+    h[e / 2] = p.x;
+    l[e / 2] = p.y;
   }
   const size_t o = static_cast<size_t>(u) * C + c;
   *reinterpret_cast<uint4*>(hi + o) = make_uint4(h[0], h[1], h[2], h[3]);
@@ -856,6 +902,7 @@ struct Work {
   float* act[8] = {};  // X, F, S1, S2, R0, R1, R2, T1
   float *sine_wavs = nullptr, *mag = nullptr, *pha = nullptr, *raw = nullptr, *stage = nullptr;
   bf16 *ahi = nullptr, *alo = nullptr;  // split A operands of the tensor-core convs
+  bf16 *bhi = nullptr, *blo = nullptr;  // second set (resblocks ping-pong between the two)
   int* err = nullptr;
 };
 
@@ -1048,7 +1095,8 @@ void free_work(Work& w) {
                    reinterpret_cast<void**>(&w.vw),    reinterpret_cast<void**>(&w.audio),
                    reinterpret_cast<void**>(&w.sine_wavs), reinterpret_cast<void**>(&w.mag),
                    reinterpret_cast<void**>(&w.pha),   reinterpret_cast<void**>(&w.raw), reinterpret_cast<void**>(&w.stage),
-                   reinterpret_cast<void**>(&w.ahi),   reinterpret_cast<void**>(&w.alo), reinterpret_cast<void**>(&w.err)};
+                   reinterpret_cast<void**>(&w.ahi),   reinterpret_cast<void**>(&w.alo), reinterpret_cast<void**>(&w.err),
+                   reinterpret_cast<void**>(&w.bhi),   reinterpret_cast<void**>(&w.blo)};
   for (void** p : ptrs) wfree(*p);
   for (float*& p : w.act) {
     void* v = p;
@@ -1079,7 +1127,7 @@ int ensure_work(lx_hift* h, int T, bool dbg) {
             A(&w.melT, static_cast<size_t>(IN_CH) * nT) && A(&w.f0, nT) && A(&w.cums, static_cast<size_t>(HARM) * nT) &&
             A(&w.bank, L_S * HARM) && A(&w.rand, HARM) && A(&w.s, L_S) && A(&w.stft, N * OUT_CH) &&
             A(&w.post, N * OUT_CH) && A(&w.vw, N * N_FFT) && A(&w.audio, L_S) && A(&w.ahi, split_elems(nT)) &&
-            A(&w.alo, split_elems(nT)) && A(&w.err, 1);
+            A(&w.alo, split_elems(nT)) && A(&w.bhi, act_floats(nT)) && A(&w.blo, act_floats(nT)) && A(&w.err, 1);
   for (int i = 0; ok && i < 8; ++i) ok = A(&w.act[i], act_floats(nT));
   if (ok && nd)
     ok = A(&w.sine_wavs, L_S * HARM) && A(&w.mag, N * N_BINS) && A(&w.pha, N * N_BINS) && A(&w.raw, L_S) &&
@@ -1117,40 +1165,69 @@ bool use_tc() {
   return v == 1;
 }
 
+// The next conv's A operands, written by a tensor-core conv's epilogue.
+struct NextSplit {
+  bf16* hi = nullptr;
+  bf16* lo = nullptr;
+  int act = ACT_NONE;
+  float slope = 0.f;
+  const SnakeW* sn = nullptr;
+};
+
+void split(cudaStream_t s, const float* in, int L_in, int C, int up, int act, float slope, const SnakeW* sn, bf16* hi,
+           bf16* lo) {
+  const size_t n8 = static_cast<size_t>(L_in) * up * C / 8;
+  k_split<<<nblk(n8, 256), 256, 0, s>>>(in, L_in, C, up, act, slope, sn ? sn->alpha : nullptr, sn ? sn->inv : nullptr,
+                                        hi, lo);
+}
+
+// Tensor-core conv over already split A operands (rows_a rows of C_in).
+// out may be null when nx carries the only consumer.  False when a tensor
+// map cannot be encoded.
+bool tc_conv(cudaStream_t s, const Work& ws, const bf16* ahi, const bf16* alo, size_t rows_a, int C_in, const ConvW& w,
+             int dil, int pad_left, const float* res, float* out, int L_out, const NextSplit* nx) {
+  const int sms = num_sms_hift();
+  CUtensorMap ah, al;
+  if (!tmap_bf16(&ah, ahi, rows_a, C_in, C_in, 128, 64) || !tmap_bf16(&al, alo, rows_a, C_in, C_in, 128, 64))
+    return false;
+  TcConvArgs ta;
+  ta.L_out = L_out;
+  ta.C_out = w.C_out_pad;
+  ta.ldo = w.C_out;
+  ta.K_taps = w.K;
+  ta.dil = dil;
+  ta.pad_left = pad_left;
+  ta.n_cb = C_in / 64;
+  ta.bias = w.b;
+  ta.res = res;
+  ta.out = out;
+  ta.err = ws.err;
+  ta.nhi = nx ? nx->hi : nullptr;
+  ta.nlo = nx ? nx->lo : nullptr;
+  ta.nact = nx ? nx->act : ACT_NONE;
+  ta.nslope = nx ? nx->slope : 0.f;
+  ta.nalpha = nx && nx->sn ? nx->sn->alpha : nullptr;
+  ta.ninv = nx && nx->sn ? nx->sn->inv : nullptr;
+  const int tiles_m = static_cast<int>(nblk(static_cast<size_t>(L_out), 128));
+  if (w.C_out_pad % 128 == 0 && tiles_m * (w.C_out_pad / 128) >= sms) {
+    const int tiles = tiles_m * (w.C_out_pad / 128);
+    k_hconv_tc<128><<<std::min(tiles, sms), TC_THREADS, tc_smem_bytes<128>(), s>>>(ah, al, w.tmh[1], w.tml[1], ta);
+  } else {
+    const int tiles = tiles_m * (w.C_out_pad / 64);
+    k_hconv_tc<64><<<std::min(tiles, sms), TC_THREADS, tc_smem_bytes<64>(), s>>>(ah, al, w.tmh[0], w.tml[0], ta);
+  }
+  return true;
+}
+
 // One conv of the network (see ConvArgs for the semantics).  Returns false
 // when a tensor map cannot be encoded.
 bool hconv(cudaStream_t s, const Work& ws, const float* in, int L_in, int C_in, int up, const ConvW& w, int dil,
            int pad_left, int act, float slope, const SnakeW* sn, const float* res, float* out, int L_out) {
   const int sms = num_sms_hift();
   if (use_tc() && w.tc && C_in % 64 == 0) {
-    const size_t rows = static_cast<size_t>(L_in) * up;
-    const size_t n8 = rows * C_in / 8;
-    k_split<<<nblk(n8, 256), 256, 0, s>>>(in, L_in, C_in, up, act, slope, sn ? sn->alpha : nullptr,
-                                          sn ? sn->inv : nullptr, ws.ahi, ws.alo);
-    CUtensorMap ah, al;
-    if (!tmap_bf16(&ah, ws.ahi, rows, C_in, C_in, 128, 64) || !tmap_bf16(&al, ws.alo, rows, C_in, C_in, 128, 64))
-      return false;
-    TcConvArgs ta;
-    ta.L_out = L_out;
-    ta.C_out = w.C_out_pad;
-    ta.ldo = w.C_out;
-    ta.K_taps = w.K;
-    ta.dil = dil;
-    ta.pad_left = pad_left;
-    ta.n_cb = C_in / 64;
-    ta.bias = w.b;
-    ta.res = res;
-    ta.out = out;
-    ta.err = ws.err;
-    const int tiles_m = static_cast<int>(nblk(static_cast<size_t>(L_out), 128));
-    if (w.C_out_pad % 128 == 0 && tiles_m * (w.C_out_pad / 128) >= sms) {
-      const int tiles = tiles_m * (w.C_out_pad / 128);
-      k_hconv_tc<128><<<std::min(tiles, sms), TC_THREADS, tc_smem_bytes<128>(), s>>>(ah, al, w.tmh[1], w.tml[1], ta);
-    } else {
-      const int tiles = tiles_m * (w.C_out_pad / 64);
-      k_hconv_tc<64><<<std::min(tiles, sms), TC_THREADS, tc_smem_bytes<64>(), s>>>(ah, al, w.tmh[0], w.tml[0], ta);
-    }
-    return true;
+    split(s, in, L_in, C_in, up, act, slope, sn, ws.ahi, ws.alo);
+    return tc_conv(s, ws, ws.ahi, ws.alo, static_cast<size_t>(L_in) * up, C_in, w, dil, pad_left, res, out, L_out,
+                   nullptr);
   }
   ConvArgs a;
   a.in = in;
@@ -1185,6 +1262,30 @@ bool hconv(cudaStream_t s, const Work& ws, const float* in, int L_in, int C_in, 
 
 // resblock (hift.cpp:25-40): R = x after 3 x (snake1 -> conv1(d_j) -> snake2 -> conv2 + residual)
 bool resblock(cudaStream_t s, const Work& ws, const ResW& w, int k, const float* X, float* R, float* T1, int C, int L) {
+  if (use_tc() && w.c1[0].tc && C % 64 == 0) {
+    // split(snake1_0(X)) once; afterwards every conv's epilogue writes the
+    // next conv's split operands (conv1 -> snake2 of its output, no fp32
+    // copy; conv2 -> the residual sum R and snake1_{j+1}(R)), ping-ponging
+    // between the two split buffers
+    split(s, X, L, C, 1, ACT_SNAKE, 0.f, &w.a1[0], ws.ahi, ws.alo);
+    for (int j = 0; j < 3; ++j) {
+      const int d = RESBLOCK_DILATIONS[j];
+      NextSplit n1;
+      n1.hi = ws.bhi;
+      n1.lo = ws.blo;
+      n1.act = ACT_SNAKE;
+      n1.sn = &w.a2[j];
+      if (!tc_conv(s, ws, ws.ahi, ws.alo, L, C, w.c1[j], d, d * (k - 1), nullptr, nullptr, L, &n1)) return false;
+      NextSplit n2;
+      n2.hi = ws.ahi;
+      n2.lo = ws.alo;
+      n2.act = ACT_SNAKE;
+      n2.sn = j < 2 ? &w.a1[j + 1] : nullptr;
+      if (!tc_conv(s, ws, ws.bhi, ws.blo, L, C, w.c2[j], 1, k - 1, j == 0 ? X : R, R, L, j < 2 ? &n2 : nullptr))
+        return false;
+    }
+    return true;
+  }
   for (int j = 0; j < 3; ++j) {
     const int d = RESBLOCK_DILATIONS[j];
     const float* src = j == 0 ? X : R;
@@ -1222,10 +1323,10 @@ int forward(lx_hift* h, const float* mel_dev, int T, const float* rand, const fl
   // f0 predictor (float64)
   k_mel_prep<<<nblk(static_cast<size_t>(IN_CH) * T, 256), 256, 0, s>>>(mel_dev, T, w.mel_d, w.melT);
   const dim3 f0_grid(nblk(T, F0_BT), BASE_CH / F0_BO);
-  k_f0_conv<<<f0_grid, 256, 0, s>>>(w.mel_d, T, IN_CH, m.f0_w[0], m.f0_b[0], 4, 0, 1, w.y0);
+  k_f0_conv<4><<<f0_grid, 256, 0, s>>>(w.mel_d, T, IN_CH, m.f0_w[0], m.f0_b[0], 0, 1, w.y0);
   double *ya = w.y0, *yb = w.y1;
   for (int i = 1; i < 5; ++i) {
-    k_f0_conv<<<f0_grid, 256, 0, s>>>(ya, T, BASE_CH, m.f0_w[i], m.f0_b[i], 3, 2, 1, yb);
+    k_f0_conv<3><<<f0_grid, 256, 0, s>>>(ya, T, BASE_CH, m.f0_w[i], m.f0_b[i], 2, 1, yb);
     std::swap(ya, yb);
   }
   k_f0_cls<<<nblk(T, 128), 128, 0, s>>>(ya, T, m.cls_w, m.cls_b, w.f0);
