@@ -592,11 +592,13 @@ __global__ void k_transpose(const float* __restrict__ in, int L, int C, int act,
 // channels, B = that tap's [BN out x 64 in] weight slice.  Per 16-wide K step
 // two MMAs: A_hi x [B_hi; B_lo] (N = 2 BN, into accumulator columns
 // [0, 2BN): hh | hl) and A_lo x B_hi (N = BN, added into [0, BN)); the
-// epilogue sums the two halves.  The K loop runs over (tap, 64-channel slice):
-// the A boxes of tap t are the 128-row tiles shifted by t*dil - pad_left rows
-// (TMA rows outside the tensor read as zero: the causal padding).
-//   warp 0      TMA: A_hi, A_lo (128 x 64) and B_hi, B_lo (BN x 64, adjacent
-//               in shared memory) per stage
+// epilogue sums the two halves.  Per (tile, 64-channel slice) one A window
+// of 128 + (K-1)*dil rows is loaded (from row m0 - pad_left; TMA rows outside
+// the tensor read as zero: the causal padding) and tap t reads it from row
+// t*dil on, so the activations cross L2 once per slice instead of once per
+// tap; the taps' weight slices stream through their own ring.
+//   warp 0      TMA: A_hi, A_lo windows (2 slots) and per tap B_hi, B_lo
+//               (BN x 64, adjacent in shared memory; 6 / 3 slots)
 //   warp 1      TMEM allocator; lane 0 issues the MMAs
 //   warps 2..17 epilogue, four warps per TMEM lane quarter (each a quarter
 //               of the columns): TMEM -> registers, hh+lh + hl + bias
@@ -607,6 +609,7 @@ constexpr int TC_THREADS = 576;  // warp 0 TMA, warp 1 MMA, warps 2..17 epilogue
 
 struct TcConvArgs {
   int L_out, C_out, K_taps, dil, pad_left, n_cb;
+  int wrows;          // rows of an A window: 128 + (K_taps - 1) * dil rounded up to 8 (<= TC_WROWS_MAX)
   int ldo;            // real output channels (<= C_out, the 64-padded tile count): row stride of res / out
   const float* bias;  // [C_out]
   const float* res;   // [L_out][ldo] or null (may alias out)
@@ -632,21 +635,24 @@ __device__ __forceinline__ uint2 split_pair(float a0, float a1) {
       static_cast<uint32_t>(__bfloat16_as_ushort(l0)) | (static_cast<uint32_t>(__bfloat16_as_ushort(l1)) << 16));
 }
 
+constexpr int TC_WROWS_MAX = 184;  // A window rows: 128 + (K - 1) * dil, rounded up to 8 (K = 11, dil = 5)
+constexpr int TC_A_HALF = TC_WROWS_MAX * 128;  // one bf16 plane of a window (23 KB, 1024-aligned)
+constexpr int TC_A_SLOT = 2 * TC_A_HALF;       // hi + lo
+
 template <int BN>
-__host__ __device__ constexpr int tc_stages() { return BN == 64 ? 4 : 3; }
+__host__ __device__ constexpr int tc_bslots() { return BN == 64 ? 6 : 3; }
 template <int BN>
-__host__ __device__ constexpr int tc_stage_bytes() { return 2 * 128 * 64 * 2 + 2 * BN * 64 * 2; }
-template <int BN>
-__host__ __device__ constexpr int tc_smem_bytes() { return 1024 + tc_stages<BN>() * tc_stage_bytes<BN>() + 256; }
+__host__ __device__ constexpr int tc_smem_bytes() {
+  return 1024 + 2 * TC_A_SLOT + tc_bslots<BN>() * 2 * BN * 128 + 256;
+}
 
 template <int BN>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     k_hconv_tc(const __grid_constant__ CUtensorMap tmAh, const __grid_constant__ CUtensorMap tmAl,
                const __grid_constant__ CUtensorMap tmBh, const __grid_constant__ CUtensorMap tmBl, TcConvArgs a) {
-  constexpr int STAGES = tc_stages<BN>();
-  constexpr int A_BYTES = 128 * 64 * 2;
-  constexpr int B_BYTES = BN * 64 * 2;
-  constexpr int STAGE_BYTES = tc_stage_bytes<BN>();
+  constexpr int NBS = tc_bslots<BN>();
+  constexpr int B_BYTES = BN * 128;
+  constexpr int B_SLOT = 2 * B_BYTES;
   constexpr uint32_t ACC_COLS = 2 * BN;
   constexpr uint32_t TMEM_COLS = 4 * BN;  // two accumulators
   constexpr uint32_t IDESC_HH_HL = idesc_bf16_f32(128, 2 * BN);
@@ -655,9 +661,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
-  uint64_t* empty = full + STAGES;
-  uint64_t* tfull = empty + STAGES;
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + 2 * TC_A_SLOT;
+  uint64_t* a_full = reinterpret_cast<uint64_t*>(sB + NBS * B_SLOT);
+  uint64_t* a_empty = a_full + 2;
+  uint64_t* b_full = a_empty + 2;
+  uint64_t* b_empty = b_full + NBS;
+  uint64_t* tfull = b_empty + NBS;
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -665,13 +675,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
-    }
     for (int i = 0; i < 2; ++i) {
+      mbar_init(&a_full[i], 1);
+      mbar_init(&a_empty[i], 1);
       mbar_init(&tfull[i], 1);
       mbar_init(&tempty[i], 16);
+    }
+    for (int i = 0; i < NBS; ++i) {
+      mbar_init(&b_full[i], 1);
+      mbar_init(&b_empty[i], 1);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -693,59 +705,79 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
   const int tiles_n = a.C_out / BN;
   const int n_tiles = ((a.L_out + 127) / 128) * tiles_n;
-  const int num_kb = a.K_taps * a.n_cb;
 
   if (warp == 0) {
     if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
+      // per (tile, 64-channel slice): one A window (hi, lo) of wrows rows from
+      // row m0 - pad_left, then the K taps' weight slices through the B ring
+      int as = 0, bs = 0;
+      uint32_t aph = 0, bph = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
         const int m0 = (tile / tiles_n) * 128, n0 = (tile % tiles_n) * BN;
-        for (int kb = 0; kb < num_kb; ++kb) {
-          if (!(ok = mbar_wait(&empty[stage], phase ^ 1u, a.err, abort_flag, DEV_TIMEOUT_PRODUCER))) break;
-          const int t = kb / a.n_cb, c = kb - t * a.n_cb;
-          const int y = m0 + t * a.dil - a.pad_left;
-          uint8_t* st = smem + stage * STAGE_BYTES;
-          mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
-          tma_load_2d(st, &tmAh, &full[stage], c * 64, y);
-          tma_load_2d(st + A_BYTES, &tmAl, &full[stage], c * 64, y);
-          tma_load_2d(st + 2 * A_BYTES, &tmBh, &full[stage], c * 64, t * a.C_out + n0);
-          tma_load_2d(st + 2 * A_BYTES + B_BYTES, &tmBl, &full[stage], c * 64, t * a.C_out + n0);
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1u;
+        for (int c = 0; ok && c < a.n_cb; ++c) {
+          if (!(ok = mbar_wait(&a_empty[as], aph ^ 1u, a.err, abort_flag, DEV_TIMEOUT_PRODUCER))) break;
+          uint8_t* wa = sA + as * TC_A_SLOT;
+          mbar_arrive_expect_tx(&a_full[as], 2 * a.wrows * 128);
+          tma_load_2d(wa, &tmAh, &a_full[as], c * 64, m0 - a.pad_left);
+          tma_load_2d(wa + TC_A_HALF, &tmAl, &a_full[as], c * 64, m0 - a.pad_left);
+          if (++as == 2) {
+            as = 0;
+            aph ^= 1u;
+          }
+          for (int t = 0; t < a.K_taps; ++t) {
+            if (!(ok = mbar_wait(&b_empty[bs], bph ^ 1u, a.err, abort_flag, DEV_TIMEOUT_PRODUCER))) break;
+            uint8_t* wb = sB + bs * B_SLOT;
+            mbar_arrive_expect_tx(&b_full[bs], B_SLOT);
+            tma_load_2d(wb, &tmBh, &b_full[bs], c * 64, t * a.C_out + n0);
+            tma_load_2d(wb + B_BYTES, &tmBl, &b_full[bs], c * 64, t * a.C_out + n0);
+            if (++bs == NBS) {
+              bs = 0;
+              bph ^= 1u;
+            }
           }
         }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint64_t d0 = sdesc_sw128(smem_u32(smem));
-      int stage = 0;
-      uint32_t phase = 0;
-      int acc = 0;
-      uint32_t acc_phase = 0;
+      int as = 0, bs = 0, acc = 0;
+      uint32_t aph = 0, bph = 0, acc_phase = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
         if (!(ok = mbar_wait(&tempty[acc], acc_phase ^ 1u, a.err, abort_flag, DEV_TIMEOUT_MMA))) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc) * ACC_COLS;
-        for (int kb = 0; kb < num_kb; ++kb) {
-          if (!(ok = mbar_wait(&full[stage], phase, a.err, abort_flag, DEV_TIMEOUT_MMA))) break;
-          tc_fence_after();
-          const uint64_t dah = d0 + static_cast<uint64_t>((stage * STAGE_BYTES) >> 4);
-          const uint64_t dal = dah + static_cast<uint64_t>(A_BYTES >> 4);
-          const uint64_t dbh = dah + static_cast<uint64_t>((2 * A_BYTES) >> 4);
+        bool first = true;
+        for (int c = 0; ok && c < a.n_cb; ++c) {
+          if (!(ok = mbar_wait(&a_full[as], aph, a.err, abort_flag, DEV_TIMEOUT_MMA))) break;
+          const uint32_t wa = smem_u32(sA + as * TC_A_SLOT);
+          for (int t = 0; t < a.K_taps; ++t) {
+            if (!(ok = mbar_wait(&b_full[bs], bph, a.err, abort_flag, DEV_TIMEOUT_MMA))) break;
+            tc_fence_after();
+            // tap t reads the window from row t * dil: the 128B swizzle is a
+            // function of the absolute shared-memory address, so a view that
+            // starts at any 128-byte row is a valid operand (base offset 0)
+            const uint32_t shift = static_cast<uint32_t>(t * a.dil) * 128u;
+            const uint64_t dah = sdesc_sw128(wa + shift);
+            const uint64_t dal = sdesc_sw128(wa + TC_A_HALF + shift);
+            const uint64_t dbh = sdesc_sw128(smem_u32(sB + bs * B_SLOT));
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            umma_ss(d_tmem, dah + 2 * k, dbh + 2 * k, IDESC_HH_HL, (kb > 0 || k > 0) ? 1u : 0u);
-            umma_ss(d_tmem, dal + 2 * k, dbh + 2 * k, IDESC_LH, 1u);
+            for (int k = 0; k < 4; ++k) {
+              umma_ss(d_tmem, dah + 2 * k, dbh + 2 * k, IDESC_HH_HL, (first && k == 0) ? 0u : 1u);
+              umma_ss(d_tmem, dal + 2 * k, dbh + 2 * k, IDESC_LH, 1u);
+            }
+            first = false;
+            umma_commit(&b_empty[bs]);
+            if (++bs == NBS) {
+              bs = 0;
+              bph ^= 1u;
+            }
           }
-          umma_commit(&empty[stage]);
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1u;
+          umma_commit(&a_empty[as]);
+          if (++as == 2) {
+            as = 0;
+            aph ^= 1u;
           }
         }
         if (!ok) break;
@@ -1187,10 +1219,13 @@ void split(cudaStream_t s, const float* in, int L_in, int C, int up, int act, fl
 bool tc_conv(cudaStream_t s, const Work& ws, const bf16* ahi, const bf16* alo, size_t rows_a, int C_in, const ConvW& w,
              int dil, int pad_left, const float* res, float* out, int L_out, const NextSplit* nx) {
   const int sms = num_sms_hift();
+  const int wrows = (128 + (w.K - 1) * dil + 7) / 8 * 8;
+  if (wrows > TC_WROWS_MAX) return false;
   CUtensorMap ah, al;
-  if (!tmap_bf16(&ah, ahi, rows_a, C_in, C_in, 128, 64) || !tmap_bf16(&al, alo, rows_a, C_in, C_in, 128, 64))
+  if (!tmap_bf16(&ah, ahi, rows_a, C_in, C_in, wrows, 64) || !tmap_bf16(&al, alo, rows_a, C_in, C_in, wrows, 64))
     return false;
   TcConvArgs ta;
+  ta.wrows = wrows;
   ta.L_out = L_out;
   ta.C_out = w.C_out_pad;
   ta.ldo = w.C_out;
