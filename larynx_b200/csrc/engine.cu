@@ -656,6 +656,10 @@ void enqueue_dit(lx_flow* h, const Plan& p, const float* mod, const float* mod_f
 }
 
 void enqueue_decode_steps(lx_flow* h, const Plan& p, int steps, int chunk, cudaStream_t s) {
+  struct PdlScope {
+    explicit PdlScope(bool on) { pdl_set_auto(on); }
+    ~PdlScope() { pdl_set_auto(false); }
+  } pdl_scope(p.R <= PDL_AUTO_MAX_ROWS);
   Model& W = h->W;
   for (int st = 0; st < steps; ++st) {
     enqueue_dit(h, p, W.mod + static_cast<size_t>(st) * DEPTH * MOD_N, W.mod_final + static_cast<size_t>(st) * 2 * DIM,

@@ -26,16 +26,24 @@ int num_sms() {
   return cache[dev];
 }
 
+// Programmatic dependent launch.  Measured on the 64-utterance decode it costs
+// ~2% of throughput (dependent CTAs park on SMs the running kernel's tail
+// could use) and saves ~1 ms of the single-utterance latency, so by default
+// the engine turns it on only for small batch plans (pdl_set_auto, per
+// thread); LX_FLOW_PDL=1 / 0 forces it on / off everywhere.
+namespace {
+thread_local bool t_pdl_auto = false;
+}
+
+void pdl_set_auto(bool on) { t_pdl_auto = on; }
+
 bool pdl_enabled() {
-  static int on = -1;
-  if (on < 0) {
-    // opt-in: measured on the 64-utterance decode PDL costs ~2% of throughput
-    // (dependent CTAs park on SMs the running kernel's tail could use) and
-    // saves ~1 ms of the single-utterance latency
+  static int env = -2;
+  if (env == -2) {
     const char* e = getenv("LX_FLOW_PDL");
-    on = (e && e[0] == '1') ? 1 : 0;
+    env = (e && e[0] == '1') ? 1 : (e && e[0] == '0') ? 0 : -1;
   }
-  return on != 0;
+  return env >= 0 ? env != 0 : t_pdl_auto;
 }
 
 int rows_per_block(int R) {

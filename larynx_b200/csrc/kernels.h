@@ -34,6 +34,11 @@ int num_sms();
 // waits for it inside before touching memory.
 // LX_FLOW_PDL=1 in the environment turns the attribute on (off by default).
 bool pdl_enabled();
+// Per-thread default of pdl_enabled() when LX_FLOW_PDL is unset.
+void pdl_set_auto(bool on);
+// Batch plans of at most this many packed rows launch with PDL by default
+// (latency-bound: the single 20 s utterance is 2 x 1000 rows).
+constexpr int PDL_AUTO_MAX_ROWS = 16384;
 // Rows per block of the warp-per-row kernels (LX_FLOW_ROWS_PER_BLOCK, default
 // 8; 0 = as many as spread a small batch over every SM in one wave, <= 16).
 int rows_per_block(int R);
