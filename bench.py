@@ -307,7 +307,7 @@ def bench_cfg4(dec, dev, stream, streams=256, iters=3):
     return out
 
 
-def bench_hift(dev, T=1000, iters=5):
+def bench_hift(dev, T=1000, iters=5, with_cpu=True):
     """HiFT vocoder (the stage after the Flow decoder) on one 20 s utterance:
     mel [80][T] in HBM -> 24 kHz audio, device-timed, synthetic weights and
     source bank.  The conv network runs in float32 on the CUDA cores; its
@@ -347,10 +347,26 @@ def bench_hift(dev, T=1000, iters=5):
     fl = conv_flops(T)
     bf16 = load_peaks()["tensor"]
     ach = fl / (ms * 1e-3) / 1e12
+    cpu = None
+    if with_cpu:
+        # the oracle port on the host cores (the reference's own HiFT runs its
+        # conv network through GGML, which is not buildable here)
+        from larynx_b200.hift_weights import synthetic_weights
+        from oracle import hift_oracle as ho
+        Tc = 100
+        w = synthetic_weights(0)
+        ri, bank = synthetic_source(1, Tc * 480)
+        melc = np.random.default_rng(6).standard_normal((80, Tc)).astype(np.float32)
+        t0 = time.perf_counter()
+        ho.vocode(melc, ri, bank, w)
+        sec = time.perf_counter() - t0
+        cpu = {"value": round(Tc / sec, 1), "unit": "mel-frames/s", "cores": cpu_cores(), "kind": "port",
+               "sample": f"1 utterance x {Tc} frames (numpy restatement of the reference's HiFT, oracle/)"}
     return {"T_frames": T, "audio_s": T * 480 / 24000, "ms": round(ms, 3),
             "mel_frames_per_s": round(T / (ms * 1e-3), 1), "rtf": (ms * 1e-3) / (T * 480 / 24000),
             "conv_tflops_fp32_equiv": round(ach, 2),
             "ceiling_tflops": round(bf16 / 3, 1), "frac_of_ceiling": round(ach / (bf16 / 3), 3),
+            "cpu_baseline": cpu,
             "finite": bool(torch.isfinite(audio).all().item()),
             "about": "whole vocoder (f0 fp64, SineGen2, STFT, conv network, ISTFT) per call; the convs with "
                      "64-multiple channel counts run on tcgen05 with a 3-term bf16 split (3 bf16 products per "
@@ -566,7 +582,7 @@ def run_ours(args):
     if not args.no_cfg4:
         extra["cfg4_stream"] = bench_cfg4(dec, dev, stream)
     if world == 1 and not args.no_hift:
-        extra["hift"] = bench_hift(dev)
+        extra["hift"] = bench_hift(dev, with_cpu=not args.no_cpu)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -615,7 +631,7 @@ def main():
         ap.error("--warmup must be >= 3")
     if args.only_hift:
         import torch
-        print(json.dumps(bench_hift(torch.device("cuda", 0))))
+        print(json.dumps(bench_hift(torch.device("cuda", 0), with_cpu=not args.no_cpu)))
         return
     if args.impl == "reference":
         run_reference(args)
