@@ -35,6 +35,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <map>
 #include <memory>
 #include <string>
 #include <vector>
@@ -950,6 +951,10 @@ struct lx_hift {
   float* d_rand_ini = nullptr;  // [9]
   float* d_bank = nullptr;      // [SINE_MAX_SAMPLES][9]
   lx::hift::Work ws;
+  // whole-vocode CUDA graphs (no debug captures), keyed by T and the source
+  // buffers; dropped whenever the workspace is reallocated
+  std::map<std::string, cudaGraphExec_t> graphs;
+  bool use_graphs = true;
   std::string err;
   int fail(int code, const std::string& msg) {
     err = msg;
@@ -1143,10 +1148,16 @@ size_t act_floats(int T) { return static_cast<size_t>(7680) * T + 64; }
 // largest tensor-core A operand: the x3 upsampled 128-channel input of ups.2
 size_t split_elems(int T) { return static_cast<size_t>(15360) * T + 64; }
 
+void clear_graphs(lx_hift* h) {
+  for (auto& kv : h->graphs) cudaGraphExecDestroy(kv.second);
+  h->graphs.clear();
+}
+
 int ensure_work(lx_hift* h, int T, bool dbg) {
   Work& w = h->ws;
   if (w.cap_T >= T && (w.cap_dbg || !dbg)) return LX_OK;
   cudaStreamSynchronize(h->stream);
+  clear_graphs(h);
   const int nT = std::max(T, w.cap_T);
   const bool nd = dbg || w.cap_dbg;
   free_work(w);
@@ -1447,6 +1458,40 @@ int forward(lx_hift* h, const float* mel_dev, int T, const float* rand, const fl
   return LX_OK;
 }
 
+// forward() on stream s, replayed from a CUDA graph when no debug capture is
+// asked for (the ~120 launches of a call then cost one graph launch).  The
+// graph reads mel from the workspace, so callers copy it there first.
+int run_forward(lx_hift* h, int T, const float* rand, const float* bank, cudaStream_t s, lx_hift_debug* dbg) {
+  if (dbg || !h->use_graphs) return forward(h, h->ws.mel, T, rand, bank, s, dbg);
+  char key[96];
+  std::snprintf(key, sizeof key, "%d|%p|%p", T, static_cast<const void*>(rand), static_cast<const void*>(bank));
+  auto it = h->graphs.find(key);
+  if (it == h->graphs.end()) {
+    cudaStream_t cs;
+    HCK(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking));
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal);
+    int rc = LX_OK;
+    if (e == cudaSuccess) {
+      rc = forward(h, h->ws.mel, T, rand, bank, cs, nullptr);
+      e = cudaStreamEndCapture(cs, &g);
+    }
+    cudaStreamDestroy(cs);
+    if (rc != LX_OK || e != cudaSuccess) {
+      if (g) cudaGraphDestroy(g);
+      cudaGetLastError();
+      return rc != LX_OK ? rc : cuda_fail(h, e, "hift graph capture");
+    }
+    cudaGraphExec_t ex = nullptr;
+    e = cudaGraphInstantiate(&ex, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return cuda_fail(h, e, "hift graph instantiate");
+    it = h->graphs.emplace(key, ex).first;
+  }
+  HCK(cudaGraphLaunch(it->second, s));
+  return LX_OK;
+}
+
 int upload_dft(lx_hift* h) {
   DftConst d;
   for (int f = 0; f < N_FFT; ++f)
@@ -1482,6 +1527,8 @@ extern "C" int lx_hift_create(int device, lx_hift** out) {
   if (cudaSetDevice(device) != cudaSuccess) return LX_ERR_CUDA;
   std::unique_ptr<lx_hift> h(new lx_hift());
   h->device = device;
+  const char* ge = std::getenv("LX_HIFT_GRAPHS");
+  if (ge && std::strcmp(ge, "0") == 0) h->use_graphs = false;
   if (cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking) != cudaSuccess) return LX_ERR_CUDA;
   if (lx::hift::upload_dft(h.get()) != LX_OK) return LX_ERR_CUDA;
   if (cudaFuncSetAttribute(lx::hift::k_hconv_tc<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1497,6 +1544,7 @@ extern "C" void lx_hift_destroy(lx_hift* h) {
   if (!h) return;
   cudaSetDevice(h->device);
   cudaStreamSynchronize(h->stream);
+  lx::hift::clear_graphs(h);
   lx::hift::free_work(h->ws);
   for (void* p : h->allocs) cudaFree(p);
   if (h->d_bank) cudaFree(h->d_bank);
@@ -1588,7 +1636,7 @@ extern "C" int lx_hift_vocode(lx_hift* h, const float* mel, int T, const float* 
     rand = w.rand;
     bank = w.bank;
   }
-  if (int rc = lx::hift::forward(h, w.mel, T, rand, bank, s, debug)) return rc;
+  if (int rc = lx::hift::run_forward(h, T, rand, bank, s, debug)) return rc;
   VCK(cudaMemcpyAsync(audio, w.audio, L_S * sizeof(float), cudaMemcpyDeviceToHost, s));
   int dev_err = 0;
   VCK(cudaMemcpyAsync(&dev_err, w.err, sizeof(int), cudaMemcpyDeviceToHost, s));
@@ -1609,7 +1657,10 @@ extern "C" int lx_hift_vocode_device(lx_hift* h, const float* mel_dev, int T, fl
   cudaSetDevice(h->device);
   if (int rc = lx::hift::ensure_work(h, T, false)) return rc;
   cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : h->stream;
-  if (int rc = lx::hift::forward(h, mel_dev, T, h->d_rand_ini, h->d_bank, s, nullptr)) return rc;
+  if (cudaMemcpyAsync(h->ws.mel, mel_dev, static_cast<size_t>(lx::hift::IN_CH) * T * sizeof(float),
+                      cudaMemcpyDeviceToDevice, s) != cudaSuccess)
+    return h->fail(LX_ERR_CUDA, "hift: input copy failed");
+  if (int rc = lx::hift::run_forward(h, T, h->d_rand_ini, h->d_bank, s, nullptr)) return rc;
   if (cudaMemcpyAsync(audio_dev, h->ws.audio, L_S * sizeof(float), cudaMemcpyDeviceToDevice, s) != cudaSuccess)
     return h->fail(LX_ERR_CUDA, "hift: output copy failed");
   return LX_OK;
