@@ -789,9 +789,30 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
   } else {
     // epilogue warps 2..17 -> TMEM lane quarter warp % 4; warps 2..5 take
-    // columns [0, BN/4), 6..9 [BN/4, BN/2), ...
+    // columns [0, BN/4), 6..9 [BN/4, BN/2), ...  The residual rows of the
+    // next tile are loaded into registers while this tile is finished, so
+    // their latency is off the epilogue's path (the next tile's output rows
+    // are written only by this warp, later, so an in-place residual is safe).
+    constexpr int NCH = BN / 64;  // 16-column chunks per warp
     const int q = warp & 3;
     const int cbeg = ((warp - 2) >> 2) * (BN / 4);
+    const bool vec = a.res && (a.ldo & 3) == 0;
+    float4 rres[NCH][4];
+    auto load_res = [&](int tile_) {
+      if (!vec || tile_ >= n_tiles) return;
+      const int row_ = (tile_ / tiles_n) * 128 + q * 32 + lane;
+      const int n0_ = (tile_ % tiles_n) * BN;
+#pragma unroll
+      for (int ch = 0; ch < NCH; ++ch) {
+        const int col_ = n0_ + cbeg + 16 * ch;
+        if (row_ < a.L_out && col_ + 16 <= a.ldo) {
+          const float4* rp = reinterpret_cast<const float4*>(a.res + static_cast<size_t>(row_) * a.ldo + col_);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) rres[ch][j] = rp[j];
+        }
+      }
+    };
+    load_res(blockIdx.x);
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
@@ -801,8 +822,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       tc_fence_after();
       const int row = m0 + q * 32 + lane;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc) * ACC_COLS;
-#pragma unroll 1
-      for (int c0 = cbeg; c0 < cbeg + BN / 4; c0 += 16) {
+#pragma unroll
+      for (int ch = 0; ch < NCH; ++ch) {
+        const int c0 = cbeg + 16 * ch;
         float u[16], v[16];
         tmem_ld16(t_row + c0, u);
         tmem_ld16(t_row + BN + c0, v);
@@ -824,8 +846,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           float w[16];
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (a.res) r = *reinterpret_cast<const float4*>(a.res + o + 4 * j);
+            const float4 r = vec ? rres[ch][j] : make_float4(0.f, 0.f, 0.f, 0.f);
             const float4 b = *reinterpret_cast<const float4*>(a.bias + col + 4 * j);
             w[4 * j + 0] = __fadd_rn(__fadd_rn(__fadd_rn(u[4 * j + 0], v[4 * j + 0]), b.x), r.x);
             w[4 * j + 1] = __fadd_rn(__fadd_rn(__fadd_rn(u[4 * j + 1], v[4 * j + 1]), b.y), r.y);
@@ -853,6 +874,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
+      load_res(tile + gridDim.x);
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
