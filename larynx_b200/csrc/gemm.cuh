@@ -8,7 +8,8 @@
 //   warp 1      TMEM allocator; lane 0 issues tcgen05.mma (M=128, N=BN, K=16)
 //               and tcgen05.commit to release ring slots / publish tiles
 //   warps 2..5  epilogue: tcgen05.ld of a 32-row TMEM lane quarter each,
-//               fused element-wise epilogue, direct global stores
+//               fused element-wise epilogue, direct global stores (MODE_CONV:
+//               warps 2..17, four per lane quarter, 16 columns each)
 // The fp32 accumulator is double-buffered in tensor memory (2 x BN columns),
 // so the epilogue of tile i overlaps the MMAs of tile i+1.
 //
@@ -45,7 +46,13 @@ __host__ __device__ constexpr int tmem_cols_for(int bn) {
   return (2 * bn) <= 32 ? 32 : (2 * bn) <= 64 ? 64 : (2 * bn) <= 128 ? 128 : (2 * bn) <= 256 ? 256 : 512;
 }
 
-__host__ __device__ constexpr int gemm_threads(int mode) { return mode == MODE_RESID ? 224 : GEMM_THREADS; }
+// Epilogue warps: 4 (one per TMEM lane quarter); MODE_CONV uses 16 (four per
+// quarter, 16 columns each): its Mish epilogue, not the N = 64 MMAs, bounded
+// the conv with 4 (ncu: tensor pipe 21% busy, 6 warps per SM).
+__host__ __device__ constexpr int gemm_epi_warps(int mode) { return mode == MODE_CONV ? 16 : 4; }
+__host__ __device__ constexpr int gemm_threads(int mode) {
+  return mode == MODE_RESID ? 224 : 64 + 32 * gemm_epi_warps(mode);
+}
 
 template <int BN, int STAGES, int MODE = MODE_GEMM>
 __host__ __device__ constexpr int gemm_smem_bytes() {
@@ -116,7 +123,7 @@ __global__ void __launch_bounds__(gemm_threads(MODE), 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 4);
+      mbar_init(&tempty[a], gemm_epi_warps(MODE));
     }
     mbar_init(x_full, 1);
     mbar_init(x_empty, 4);
@@ -211,7 +218,7 @@ __global__ void __launch_bounds__(gemm_threads(MODE), 1)
         if (acc == 0) acc_phase ^= 1u;
       }
     }
-  } else if (warp == 6) {
+  } else if (RES && warp == 6) {
     // residual loader (MODE_RESID only): the 128 x BN fp32 tile of the residual
     if (RES && lane == 0) {
       uint32_t xph = 0;
@@ -241,20 +248,30 @@ __global__ void __launch_bounds__(gemm_threads(MODE), 1)
       const int rt = q * 32 + lane;  // row inside the tile
       const int row = m0 + rt;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
-      // software-pipelined: the TMEM load of chunk c+1 is in flight while
-      // chunk c is processed (tcgen05.wait::ld waits for all of this thread's loads)
-      float va[16], vb[16];
-      tmem_ld16(t_row, va);
-      tmem_ld_wait();
-#pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
-        if (c0 + 16 < BN) tmem_ld16(t_row + c0 + 16, vb);
+      if constexpr (MODE == MODE_CONV) {
+        // warps 2..17: lane quarter warp % 4, columns [16 g, 16 g + 16) for g = (warp - 2) / 4
+        static_assert(MODE != MODE_CONV || BN == 64, "MODE_CONV tiles are 64 channels wide");
+        const int c0 = ((warp - 2) >> 2) * 16;
+        float va[16];
+        tmem_ld16(t_row + c0, va);
+        tmem_ld_wait();
         epi_chunk<RES>(epi, sX, rt, row, n0, c0, sh, va);
+      } else {
+        // software-pipelined: the TMEM load of chunk c+1 is in flight while
+        // chunk c is processed (tcgen05.wait::ld waits for all of this thread's loads)
+        float va[16], vb[16];
+        tmem_ld16(t_row, va);
         tmem_ld_wait();
-        if (c0 + 16 >= BN) break;
-        if (c0 + 32 < BN) tmem_ld16(t_row + c0 + 32, va);
-        epi_chunk<RES>(epi, sX, rt, row, n0, c0 + 16, sh, vb);
-        tmem_ld_wait();
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+          if (c0 + 16 < BN) tmem_ld16(t_row + c0 + 16, vb);
+          epi_chunk<RES>(epi, sX, rt, row, n0, c0, sh, va);
+          tmem_ld_wait();
+          if (c0 + 16 >= BN) break;
+          if (c0 + 32 < BN) tmem_ld16(t_row + c0 + 32, va);
+          epi_chunk<RES>(epi, sX, rt, row, n0, c0 + 16, sh, vb);
+          tmem_ld_wait();
+        }
       }
       tc_fence_before();
       __syncwarp();
