@@ -311,9 +311,16 @@ __device__ __forceinline__ float gelu_tanh_fast(float x) {
 }
 
 // Mish = x * tanh(softplus(x)); softplus with torch's threshold 20.
+// Mish x * tanh(softplus(x)) through the identity
+//   tanh(log(1 + n)) = (n^2 + 2n) / (n^2 + 2n + 2),  n = e^x,
+// one exponential and one division instead of exp, log1p and tanh (the
+// conv-pos epilogue evaluates it for every output).  Above x = 20 the factor
+// is 1 in fp32; far below 0, n -> 0 and the result -> x * n.
 __device__ __forceinline__ float mish_f(float x) {
-  const float sp = x > 20.0f ? x : log1pf(expf(x));
-  return x * tanhf(sp);
+  if (x > 20.0f) return x;
+  const float n = __expf(x);
+  const float t = n * (n + 2.0f);
+  return x * __fdividef(t, t + 2.0f);
 }
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }

@@ -517,8 +517,8 @@ int ensure_workspace(lx_flow* h, const Plan& p, size_t in_floats, int n_utt) {
     ok &= tmap_bf16(&w.tm_h, w.h, R, FF, FF, 128, 64);
     ok &= tmap_bf16(&w.tm_xb, w.xb, R, MEL, MEL, 128, 64);
     ok &= tmap_bf16(&w.tm_acond, w.a_cond, R, COND_K, COND_K, 128, 64);
-    ok &= tmap_bf16(&w.tm_stage1, w.stage1, Rs, DIM, DIM, 128, 64);
-    ok &= tmap_bf16(&w.tm_stage2, w.stage2, Rs, DIM, DIM, 128, 64);
+    ok &= tmap_bf16(&w.tm_stage1, w.stage1, Rs, DIM, DIM, CONV_WIN_ROWS, 64);
+    ok &= tmap_bf16(&w.tm_stage2, w.stage2, Rs, DIM, DIM, CONV_WIN_ROWS, 64);
     ok &= tmap_bf16(&w.tm_q, w.q, R, DIM, DIM, 128, 64);
     ok &= tmap_bf16(&w.tm_k, w.k, R, DIM, DIM, 128, 64);
     ok &= tmap_bf16(&w.tm_v, w.v, R, DIM, DIM, 128, 64);

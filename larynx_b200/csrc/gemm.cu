@@ -420,7 +420,19 @@ void gemm_in_proj(int bn, const CUtensorMap& A, const CUtensorMap& B, int M, con
 void conv_pos(const CUtensorMap& A, const CUtensorMap& B, int Ms, const float* bias, int second, bf16* out_stage,
               float* x, const int* s2p, int* err, cudaStream_t s) {
   EpiConv e{bias, second, out_stage, x, s2p};
-  launch<64, 8, MODE_CONV>(A, B, Ms, DIM, 0, 0, e, err, s);
+  constexpr int smem = conv_win_smem_bytes();
+  static bool attr_done[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_done[dev & 63]) {
+    cudaFuncSetAttribute(k_conv_win<EpiConv>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    attr_done[dev & 63] = true;
+  }
+  const int tiles = ((Ms + GEMM_BM - 1) / GEMM_BM) * (DIM / 64);
+  const int grid = tiles < num_sms() ? tiles : num_sms();
+  if (grid <= 0) return;
+  GemmShape sh{Ms, DIM, 0, 0, err};
+  launch_pdl(k_conv_win<EpiConv>, dim3(grid), dim3(CONV_THREADS), smem, s, A, B, sh, e);
 }
 
 }  // namespace lx

@@ -8,8 +8,7 @@
 //   warp 1      TMEM allocator; lane 0 issues tcgen05.mma (M=128, N=BN, K=16)
 //               and tcgen05.commit to release ring slots / publish tiles
 //   warps 2..5  epilogue: tcgen05.ld of a 32-row TMEM lane quarter each,
-//               fused element-wise epilogue, direct global stores (MODE_CONV:
-//               warps 2..17, four per lane quarter, 16 columns each)
+//               fused element-wise epilogue, direct global stores
 // The fp32 accumulator is double-buffered in tensor memory (2 x BN columns),
 // so the epilogue of tile i overlaps the MMAs of tile i+1.
 //
@@ -17,19 +16,16 @@
 // (128 x BN, as 32-column 128B-swizzled boxes) into shared memory while the
 // tile's MMAs run; the epilogue reads it from there instead of waiting on HBM.
 //
-// MODE_CONV turns the same pipeline into the causal grouped Conv1d of the
-// DiT's position embedding (k = 31, 16 groups of 64 channels): the K loop runs
-// over the 31 taps, the A box of tap k is the 128-row activation tile shifted
-// by k - 30 rows (TMA row coordinate; rows before the buffer start read as
-// zero, rows before each sequence are zero gap rows of the staging layout),
-// and the B box is the [64 out x 64 in] weight slice of (group, tap).
+// The causal grouped Conv1d of the DiT's position embedding runs in its own
+// kernel below (k_conv_win): one A window per tile, taps as shifted views.
 #pragma once
 
 #include "common.cuh"
+#include "kernels.h"
 
 namespace lx {
 
-enum GemmMode : int { MODE_GEMM = 0, MODE_CONV = 1, MODE_RESID = 2 };
+enum GemmMode : int { MODE_GEMM = 0, MODE_RESID = 2 };
 
 constexpr int GEMM_BM = 128;
 constexpr int GEMM_BK = 64;
@@ -46,13 +42,7 @@ __host__ __device__ constexpr int tmem_cols_for(int bn) {
   return (2 * bn) <= 32 ? 32 : (2 * bn) <= 64 ? 64 : (2 * bn) <= 128 ? 128 : (2 * bn) <= 256 ? 256 : 512;
 }
 
-// Epilogue warps: 4 (one per TMEM lane quarter); MODE_CONV uses 16 (four per
-// quarter, 16 columns each): its Mish epilogue, not the N = 64 MMAs, bounded
-// the conv with 4 (ncu: tensor pipe 21% busy, 6 warps per SM).
-__host__ __device__ constexpr int gemm_epi_warps(int mode) { return mode == MODE_CONV ? 16 : 4; }
-__host__ __device__ constexpr int gemm_threads(int mode) {
-  return mode == MODE_RESID ? 224 : 64 + 32 * gemm_epi_warps(mode);
-}
+__host__ __device__ constexpr int gemm_threads(int mode) { return mode == MODE_RESID ? 224 : GEMM_THREADS; }
 
 template <int BN, int STAGES, int MODE = MODE_GEMM>
 __host__ __device__ constexpr int gemm_smem_bytes() {
@@ -123,7 +113,7 @@ __global__ void __launch_bounds__(gemm_threads(MODE), 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], gemm_epi_warps(MODE));
+      mbar_init(&tempty[a], 4);
     }
     mbar_init(x_full, 1);
     mbar_init(x_empty, 4);
@@ -149,7 +139,7 @@ __global__ void __launch_bounds__(gemm_threads(MODE), 1)
   const int tiles_n = (sh.N + BN - 1) / BN;
   const int tiles_m = (sh.M + GEMM_BM - 1) / GEMM_BM;
   const int n_tiles = tiles_m * tiles_n;
-  const int num_kb = (MODE == MODE_CONV) ? CONV_TAPS : (sh.K + GEMM_BK - 1) / GEMM_BK;
+  const int num_kb = (sh.K + GEMM_BK - 1) / GEMM_BK;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -165,14 +155,8 @@ __global__ void __launch_bounds__(gemm_threads(MODE), 1)
             break;
           }
           mbar_arrive_expect_tx(&full[stage], A_BYTES + B_BYTES);
-          if (MODE == MODE_CONV) {
-            // group g = n0 / 64; tap kb
-            tma_load_2d(sA + stage * A_BYTES, &tmA, &full[stage], n0, m0 - (CONV_TAPS - 1) + kb);
-            tma_load_2d(sB + stage * B_BYTES, &tmB, &full[stage], 0, sh.b_off + ((n0 / 64) * CONV_TAPS + kb) * 64);
-          } else {
-            tma_load_2d(sA + stage * A_BYTES, &tmA, &full[stage], kb * GEMM_BK, m0);
-            tma_load_2d(sB + stage * B_BYTES, &tmB, &full[stage], kb * GEMM_BK, sh.b_off + n0);
-          }
+          tma_load_2d(sA + stage * A_BYTES, &tmA, &full[stage], kb * GEMM_BK, m0);
+          tma_load_2d(sB + stage * B_BYTES, &tmB, &full[stage], kb * GEMM_BK, sh.b_off + n0);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
@@ -248,30 +232,20 @@ __global__ void __launch_bounds__(gemm_threads(MODE), 1)
       const int rt = q * 32 + lane;  // row inside the tile
       const int row = m0 + rt;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
-      if constexpr (MODE == MODE_CONV) {
-        // warps 2..17: lane quarter warp % 4, columns [16 g, 16 g + 16) for g = (warp - 2) / 4
-        static_assert(MODE != MODE_CONV || BN == 64, "MODE_CONV tiles are 64 channels wide");
-        const int c0 = ((warp - 2) >> 2) * 16;
-        float va[16];
-        tmem_ld16(t_row + c0, va);
-        tmem_ld_wait();
-        epi_chunk<RES>(epi, sX, rt, row, n0, c0, sh, va);
-      } else {
-        // software-pipelined: the TMEM load of chunk c+1 is in flight while
-        // chunk c is processed (tcgen05.wait::ld waits for all of this thread's loads)
-        float va[16], vb[16];
-        tmem_ld16(t_row, va);
-        tmem_ld_wait();
+      // software-pipelined: the TMEM load of chunk c+1 is in flight while
+      // chunk c is processed (tcgen05.wait::ld waits for all of this thread's loads)
+      float va[16], vb[16];
+      tmem_ld16(t_row, va);
+      tmem_ld_wait();
 #pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 32) {
-          if (c0 + 16 < BN) tmem_ld16(t_row + c0 + 16, vb);
-          epi_chunk<RES>(epi, sX, rt, row, n0, c0, sh, va);
-          tmem_ld_wait();
-          if (c0 + 16 >= BN) break;
-          if (c0 + 32 < BN) tmem_ld16(t_row + c0 + 32, va);
-          epi_chunk<RES>(epi, sX, rt, row, n0, c0 + 16, sh, vb);
-          tmem_ld_wait();
-        }
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        if (c0 + 16 < BN) tmem_ld16(t_row + c0 + 16, vb);
+        epi_chunk<RES>(epi, sX, rt, row, n0, c0, sh, va);
+        tmem_ld_wait();
+        if (c0 + 16 >= BN) break;
+        if (c0 + 32 < BN) tmem_ld16(t_row + c0 + 32, va);
+        epi_chunk<RES>(epi, sX, rt, row, n0, c0 + 16, sh, vb);
+        tmem_ld_wait();
       }
       tc_fence_before();
       __syncwarp();
@@ -285,6 +259,174 @@ __global__ void __launch_bounds__(gemm_threads(MODE), 1)
     }
   }
 
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Causal grouped Conv1d of the DiT's position embedding (k = 31, 16 groups of
+// 64 channels) with one A window per tile.  Tile = 128 staging rows x one
+// group; the 31 taps read rows kb .. kb + 127 of a 160-row window loaded once
+// from row m0 - 30 (TMA rows before the buffer read as zero; the staging
+// layout's 32 zero rows before each sequence are the causal padding).  The
+// 128B swizzle is applied on absolute shared-memory address bits, so a tap's
+// operand is the window's descriptor advanced by kb rows (kb x 128 bytes).
+// The per-tap [64 out x 64 in] weight slices stream through their own ring.
+// A traffic per tile: 20 KB instead of 31 x 16 KB.
+//   warp 0      TMA: A window (2 slots), weight slices (CONV_BSTAGES slots)
+//   warp 1      TMEM allocator; lane 0 issues tcgen05.mma (M=128, N=64, K=16)
+//   warps 2..17 epilogue, four per TMEM lane quarter, 16 columns each
+// ---------------------------------------------------------------------------
+constexpr int CONV_WIN_BYTES = CONV_WIN_ROWS * 128;
+constexpr int CONV_BSTAGES = 12;
+constexpr int CONV_THREADS = 64 + 16 * 32;
+constexpr int conv_win_smem_bytes() { return 1024 + 2 * CONV_WIN_BYTES + CONV_BSTAGES * 64 * 128 + 512; }
+
+template <class Epi>
+__global__ void __launch_bounds__(CONV_THREADS, 1)
+    k_conv_win(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmShape sh,
+               Epi epi) {
+  constexpr int BN = 64;
+  constexpr int B_BYTES = 64 * 128;
+  constexpr uint32_t TMEM_COLS = 128;  // two 64-column accumulators
+  constexpr uint32_t IDESC = idesc_bf16_f32(GEMM_BM, BN);
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + 2 * CONV_WIN_BYTES;
+  uint64_t* a_full = reinterpret_cast<uint64_t*>(sB + CONV_BSTAGES * B_BYTES);
+  uint64_t* a_empty = a_full + 2;
+  uint64_t* full = a_empty + 2;
+  uint64_t* empty = full + CONV_BSTAGES;
+  uint64_t* tfull = empty + CONV_BSTAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&a_full[i], 1);
+      mbar_init(&a_empty[i], 1);
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 16);
+    }
+    for (int i = 0; i < CONV_BSTAGES; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  pdl_launch_dependents();
+  pdl_wait();
+
+  const int tiles_n = sh.N / BN;
+  const int n_tiles = ((sh.M + GEMM_BM - 1) / GEMM_BM) * tiles_n;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int as = 0, bs = 0;
+      uint32_t aph = 0, bph = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
+        const int m0 = (tile / tiles_n) * GEMM_BM;
+        const int n0 = (tile % tiles_n) * BN;  // group g = n0 / 64
+        if (!(ok = mbar_wait(&a_empty[as], aph ^ 1u, sh.err, abort_flag, DEV_TIMEOUT_PRODUCER))) break;
+        mbar_arrive_expect_tx(&a_full[as], CONV_WIN_BYTES);
+        tma_load_2d(sA + as * CONV_WIN_BYTES, &tmA, &a_full[as], n0, m0 - (CONV_TAPS - 1));
+        if (++as == 2) {
+          as = 0;
+          aph ^= 1u;
+        }
+        for (int kb = 0; kb < CONV_TAPS; ++kb) {
+          if (!(ok = mbar_wait(&empty[bs], bph ^ 1u, sh.err, abort_flag, DEV_TIMEOUT_PRODUCER))) break;
+          mbar_arrive_expect_tx(&full[bs], B_BYTES);
+          tma_load_2d(sB + bs * B_BYTES, &tmB, &full[bs], 0, sh.b_off + ((n0 / 64) * CONV_TAPS + kb) * 64);
+          if (++bs == CONV_BSTAGES) {
+            bs = 0;
+            bph ^= 1u;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int as = 0, bs = 0, acc = 0;
+      uint32_t aph = 0, bph = 0, acc_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
+        if (!(ok = mbar_wait(&tempty[acc], acc_phase ^ 1u, sh.err, abort_flag, DEV_TIMEOUT_MMA))) break;
+        if (!(ok = mbar_wait(&a_full[as], aph, sh.err, abort_flag, DEV_TIMEOUT_MMA))) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        const uint32_t wa = smem_u32(sA + as * CONV_WIN_BYTES);
+        for (int kb = 0; kb < CONV_TAPS; ++kb) {
+          if (!(ok = mbar_wait(&full[bs], bph, sh.err, abort_flag, DEV_TIMEOUT_MMA))) break;
+          tc_fence_after();
+          const uint64_t da = sdesc_sw128(wa + static_cast<uint32_t>(kb) * 128u);
+          const uint64_t db = sdesc_sw128(smem_u32(sB + bs * B_BYTES));
+#pragma unroll
+          for (int k = 0; k < GEMM_BK / 16; ++k)
+            umma_ss(d_tmem, da + 2 * k, db + 2 * k, IDESC, (kb > 0 || k > 0) ? 1u : 0u);
+          umma_commit(&empty[bs]);
+          if (++bs == CONV_BSTAGES) {
+            bs = 0;
+            bph ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&a_empty[as]);
+        if (++as == 2) {
+          as = 0;
+          aph ^= 1u;
+        }
+        umma_commit(&tfull[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+    }
+  } else {
+    const int q = warp & 3;
+    const int c0 = ((warp - 2) >> 2) * 16;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+      const int m0 = (tile / tiles_n) * GEMM_BM;
+      const int n0 = (tile % tiles_n) * BN;
+      const bool ok = mbar_wait(&tfull[acc], acc_phase, sh.err, abort_flag, DEV_TIMEOUT_EPILOGUE);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      tc_fence_after();
+      const int rt = q * 32 + lane;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      float va[16];
+      tmem_ld16(t_row + c0, va);
+      tmem_ld_wait();
+      epi_chunk<false>(epi, nullptr, rt, m0 + rt, n0, c0, sh, va);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {

@@ -72,6 +72,10 @@ bool tmap_bf16(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, u
 bool tmap_f32(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows,
               uint32_t box_cols);
 
+// Rows of the conv-pos A window (128 output rows + 30 taps, rounded to 8):
+// the box height of the conv's staging tensor maps.
+constexpr int CONV_WIN_ROWS = 160;
+
 // Query rows per attention CTA.
 constexpr int ATT_Q_ROWS = 128;
 
