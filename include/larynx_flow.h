@@ -86,18 +86,26 @@ int lx_flow_load_layout(lx_flow* h, const char* path);
 int lx_flow_load_noise(lx_flow* h, const char* path);
 
 /* Optional per-stage captures of CFM step 1 (replaces larynx::flow::FlowDebug,
- * include/larynx/flow/flow.h:15-34).  Every pointer may be NULL; T = MEL_T.
- * Row 0 is the conditional, row 1 the CFG-zeroed row. */
+ * include/larynx/flow/flow.h:15-34: the same stages in the same order and the
+ * same PyTorch byte layouts; FlowDebug::feat is mel_out itself).  Every
+ * pointer may be NULL.  T = MEL_T; N = n_prompt + n_tokens token rows;
+ * N_pre = N (finalize) or N - 3 (the streaming call).  In the [2][...] stages
+ * row 0 is the conditional, row 1 the CFG-zeroed row.  conv_pos is taken as
+ * input_embed - input_proj in fp32 (the conv output is added to the residual
+ * in the conv kernel's epilogue, src/flow/dit.cpp:122). */
 typedef struct lx_flow_debug {
-  float* spk;         /* [80]                 */
-  float* mu;          /* [80][T]              */
-  float* cond;        /* [80][T]              */
-  float* time_embed;  /* [1024]               */
-  float* input_proj;  /* [2][T][1024]         */
-  float* input_embed; /* [2][T][1024]         */
-  float* blocks;      /* [22][2][T][1024]     */
-  float* norm_out;    /* [2][T][1024]         */
-  float* dphi;        /* [2][80][T]           */
+  float* spk;          /* [80]                 (1, 80)           */
+  float* token_embed;  /* [N][80]              (1, N, 80)        */
+  float* prelookahead; /* [N_pre][80]          (1, N_pre, 80)    */
+  float* mu;           /* [80][T]              (1, 80, T)        */
+  float* cond;         /* [80][T]              (1, 80, T)        */
+  float* time_embed;   /* [2][1024]            (2, 1024)         */
+  float* input_proj;   /* [2][T][1024]         proj before conv-pos */
+  float* conv_pos;     /* [2][T][1024]         conv-pos output   */
+  float* input_embed;  /* [2][T][1024]                           */
+  float* blocks;       /* [22][2][T][1024]     after each block  */
+  float* norm_out;     /* [2][T][1024]                           */
+  float* dphi;         /* [2][80][T]                             */
 } lx_flow_debug;
 
 /* Replaces both FlowDecoder::infer overloads (include/larynx/flow/flow.h:61-77;

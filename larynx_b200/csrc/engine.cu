@@ -1115,7 +1115,15 @@ int lx_flow_infer_ex(lx_flow* h, const int32_t* prompt_tokens, int n_prompt, con
     if (debug->mu) CK(cudaMemcpyAsync(debug->mu, h->f_mu, static_cast<size_t>(T) * MEL * 4, cudaMemcpyDeviceToHost, s));
     if (debug->cond)
       CK(cudaMemcpyAsync(debug->cond, h->f_cond, static_cast<size_t>(T) * MEL * 4, cudaMemcpyDeviceToHost, s));
-    if (debug->time_embed) CK(cudaMemcpyAsync(debug->time_embed, W.temb, DIM * 4, cudaMemcpyDeviceToHost, s));
+    if (debug->token_embed)
+      CK(cudaMemcpyAsync(debug->token_embed, h->f_emb, static_cast<size_t>(n_tok) * MEL * 4, cudaMemcpyDeviceToHost, s));
+    if (debug->prelookahead)
+      CK(cudaMemcpyAsync(debug->prelookahead, h->f_pre, static_cast<size_t>(n_pre) * MEL * 4, cudaMemcpyDeviceToHost,
+                         s));
+    // both CFG rows run at the same t, so the two rows of time_embed are equal
+    if (debug->time_embed)
+      for (int r = 0; r < 2; ++r)
+        CK(cudaMemcpyAsync(debug->time_embed + r * DIM, W.temb, DIM * 4, cudaMemcpyDeviceToHost, s));
   }
   lx_flow_batch b{};
   b.n_utt = 1;
@@ -1127,8 +1135,8 @@ int lx_flow_infer_ex(lx_flow* h, const int32_t* prompt_tokens, int n_prompt, con
   b.mel_out = w.out_mel;
   b.chunk = chunk;
   b.n_steps = 0;
-  const bool want_stages =
-      debug && (debug->input_proj || debug->input_embed || debug->blocks || debug->norm_out || debug->dphi);
+  const bool want_stages = debug && (debug->input_proj || debug->conv_pos || debug->input_embed || debug->blocks ||
+                                     debug->norm_out || debug->dphi);
   if (want_stages) {
     // step-1 captures: one estimator pass on [x; x] rows with the step-1 modulation
     Plan p = make_plan(1, &T, true, 0, 1);
@@ -1152,27 +1160,40 @@ int lx_flow_infer_ex(lx_flow* h, const int32_t* prompt_tokens, int n_prompt, con
     h->cached_valid = false;
     Plan pc = p;
     pc.F = static_cast<int>(rows2);
-    if (debug->input_proj) {
+    // conv_pos = input_embed - input_proj: both are fetched when it is asked for
+    std::vector<float> proj_tmp, embed_tmp;
+    float* proj_dst = debug->input_proj;
+    float* embed_dst = debug->input_embed;
+    if (debug->conv_pos && !proj_dst) {
+      proj_tmp.resize(rows2 * DIM);
+      proj_dst = proj_tmp.data();
+    }
+    if (debug->conv_pos && !embed_dst) {
+      embed_tmp.resize(rows2 * DIM);
+      embed_dst = embed_tmp.data();
+    }
+    if (proj_dst) {
       // input_proj = x after the in-proj GEMM, before the conv-pos residual
       gemm_in_proj(pick_bn(p.R, DIM), w.tm_xb, W.tm_winx[pick_bn(p.R, DIM) == 256], p.R, w.cst, w.x, w.stage1, w.p2s,
                    h->d_err, s);
       gather_rows(w.cap, w.x, w.seq_rows, static_cast<int>(rows2), DIM, s);
-      CK(cudaMemcpyAsync(debug->input_proj, w.cap, rows2 * DIM * 4, cudaMemcpyDeviceToHost, s));
+      CK(cudaMemcpyAsync(proj_dst, w.cap, rows2 * DIM * 4, cudaMemcpyDeviceToHost, s));
       h->launches += 2;
     }
     {
       Captures cap;
-      cap.input_embed = debug->input_embed ? w.cap : nullptr;
+      cap.input_embed = embed_dst ? w.cap : nullptr;
       cap.norm_out = debug->norm_out ? w.cap + rows2 * DIM : nullptr;
       cap.blocks_all = debug->blocks ? w.cap + 2 * rows2 * DIM : nullptr;
       enqueue_dit(h, pc, W.mod, W.mod_final, 0, s, &cap);
-      if (cap.input_embed)
-        CK(cudaMemcpyAsync(debug->input_embed, cap.input_embed, rows2 * DIM * 4, cudaMemcpyDeviceToHost, s));
+      if (cap.input_embed) CK(cudaMemcpyAsync(embed_dst, cap.input_embed, rows2 * DIM * 4, cudaMemcpyDeviceToHost, s));
       if (cap.norm_out) CK(cudaMemcpyAsync(debug->norm_out, cap.norm_out, rows2 * DIM * 4, cudaMemcpyDeviceToHost, s));
       if (cap.blocks_all)
         CK(cudaMemcpyAsync(debug->blocks, cap.blocks_all, static_cast<size_t>(DEPTH) * rows2 * DIM * 4,
                            cudaMemcpyDeviceToHost, s));
       CK(cudaStreamSynchronize(s));
+      if (debug->conv_pos)
+        for (size_t i = 0; i < rows2 * DIM; ++i) debug->conv_pos[i] = embed_dst[i] - proj_dst[i];
     }
     if (debug->dphi) {
       std::vector<float> rows(rows2 * MEL);

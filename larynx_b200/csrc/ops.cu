@@ -26,10 +26,13 @@ __global__ void k_v_to_f16(const bf16* __restrict__ v, __half* __restrict__ vh, 
   }
 }
 
+// Waits for the call's work and reads its error word, in order on `s` (a
+// plain cudaMemcpy would also wait for other blocking streams' work).
 int sync_check(cudaStream_t s, int* d_err) {
-  if (cudaStreamSynchronize(s) != cudaSuccess) return LX_ERR_CUDA;
   int e = 0;
-  if (cudaMemcpy(&e, d_err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return LX_ERR_CUDA;
+  if (cudaMemcpyAsync(&e, d_err, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+      cudaStreamSynchronize(s) != cudaSuccess)
+    return LX_ERR_CUDA;
   return e ? LX_ERR_TIMEOUT : LX_OK;
 }
 

@@ -19,7 +19,9 @@
 //
 // Set-up: the first call on a device (with that device current) resolves the
 // arrays' addresses with cudaGetSymbolAddress, which can load the module; make
-// that first call before any stream capture begins.  Later calls do no set-up.
+// that first call before any stream capture begins.  The addresses are cached
+// with the CUDA context they belong to; a call under another context (after a
+// cudaDeviceReset, say) looks them up again.
 //
 // Zero state: only the error word must start at zero; each call clears it on
 // the caller's stream before the kernels run.  Every V row the attention
@@ -31,6 +33,8 @@
 // race on it and produce wrong results; serialise them.  Each call is
 // synchronous on its stream, so calls made one after another from one thread
 // are safe.
+#include <cuda.h>
+
 #include <mutex>
 
 #include "../../include/larynx_flow.h"
@@ -56,21 +60,45 @@ struct Scratch {
 
 std::mutex g_setup_mu;
 Scratch g_scratch[kMaxDevices];
-bool g_ready[kMaxDevices] = {false};
+CUcontext g_ctx[kMaxDevices] = {nullptr};
 
-// Resolves the static arrays of the current device once.
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+
+// The driver's cuCtxGetCurrent, found once through the runtime (the library
+// does not link libcuda directly).
+CtxGetCurrentFn ctx_get_current() {
+  static CtxGetCurrentFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<CtxGetCurrentFn>(nullptr);
+    return reinterpret_cast<CtxGetCurrentFn>(p);
+  }();
+  return fn;
+}
+
+// Resolves the static arrays of the current device, once per CUDA context.
 int scratch_for_current_device(Scratch* out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return LX_ERR_CUDA;
+  CtxGetCurrentFn get = ctx_get_current();
+  CUcontext ctx = nullptr;
+  if (!get || get(&ctx) != CUDA_SUCCESS) return LX_ERR_CUDA;
+  if (!ctx) {
+    // no context current on this thread yet: cudaSetDevice makes the
+    // device's primary context current (CUDA 12 and later)
+    if (cudaSetDevice(dev) != cudaSuccess || get(&ctx) != CUDA_SUCCESS || !ctx) return LX_ERR_CUDA;
+  }
   std::lock_guard<std::mutex> lock(g_setup_mu);
-  if (!g_ready[dev]) {
+  if (g_ctx[dev] != ctx) {
     Scratch s;
     if (cudaGetSymbolAddress(reinterpret_cast<void**>(&s.v), g_v) != cudaSuccess ||
         cudaGetSymbolAddress(reinterpret_cast<void**>(&s.tiles), g_tiles) != cudaSuccess ||
         cudaGetSymbolAddress(reinterpret_cast<void**>(&s.err), g_err) != cudaSuccess)
       return LX_ERR_CUDA;
     g_scratch[dev] = s;
-    g_ready[dev] = true;
+    g_ctx[dev] = ctx;
   }
   *out = g_scratch[dev];
   return LX_OK;
@@ -120,8 +148,12 @@ extern "C" int lx_flow_op_attention_static(int n_seq, const int32_t* lengths, co
   const int n8 = rows * (DIM / 8);
   k_v_to_f16_static<<<(n8 + 255) / 256, 256, 0, s>>>(static_cast<const bf16*>(v), sc.v, n8);
   if (!attention(tq, tk, tv, sc.tiles, n_tiles, chunk, static_cast<bf16*>(out), sc.err, s)) return LX_ERR_CUDA;
-  if (cudaGetLastError() != cudaSuccess || cudaStreamSynchronize(s) != cudaSuccess) return LX_ERR_CUDA;
+  if (cudaGetLastError() != cudaSuccess) return LX_ERR_CUDA;
+  // read the error word in order on the caller's stream: a plain cudaMemcpy
+  // would also wait for the work of every other blocking stream on the device
   int e = 0;
-  if (cudaMemcpy(&e, sc.err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return LX_ERR_CUDA;
+  if (cudaMemcpyAsync(&e, sc.err, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+      cudaStreamSynchronize(s) != cudaSuccess)
+    return LX_ERR_CUDA;
   return e ? LX_ERR_TIMEOUT : LX_OK;
 }

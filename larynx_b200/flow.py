@@ -43,9 +43,13 @@ _f32p = ctypes.POINTER(ctypes.c_float)
 _i32p = ctypes.POINTER(ctypes.c_int32)
 
 
+# lx_flow_debug: the stages of larynx::flow::FlowDebug (flow.h:15-34), in order
+DEBUG_STAGES = ("spk", "token_embed", "prelookahead", "mu", "cond", "time_embed", "input_proj", "conv_pos",
+                "input_embed", "blocks", "norm_out", "dphi")
+
+
 class LxFlowDebug(ctypes.Structure):
-    _fields_ = [(n, _f32p) for n in ("spk", "mu", "cond", "time_embed", "input_proj", "input_embed", "blocks",
-                                     "norm_out", "dphi")]
+    _fields_ = [(n, _f32p) for n in DEBUG_STAGES]
 
 
 class LxFlowBatch(ctypes.Structure):
@@ -197,8 +201,11 @@ class FlowDecoder:
         dbg = None
         bufs = {}
         if debug is not None:
-            shapes = {"spk": (80,), "mu": (80, T), "cond": (80, T), "time_embed": (1024,),
-                      "input_proj": (2, T, 1024), "input_embed": (2, T, 1024), "blocks": (22, 2, T, 1024),
+            n_tok = pt.size + tk.size
+            n_pre = n_tok - (0 if finalize else PRE_LOOKAHEAD)
+            shapes = {"spk": (80,), "token_embed": (n_tok, 80), "prelookahead": (n_pre, 80), "mu": (80, T),
+                      "cond": (80, T), "time_embed": (2, 1024), "input_proj": (2, T, 1024),
+                      "conv_pos": (2, T, 1024), "input_embed": (2, T, 1024), "blocks": (22, 2, T, 1024),
                       "norm_out": (2, T, 1024), "dphi": (2, 80, T)}
             bufs = {k: np.empty(v, np.float32) for k, v in shapes.items()}
             dbg = LxFlowDebug(**{k: _ptr(v) for k, v in bufs.items()})

@@ -114,9 +114,30 @@ def test_decode_padded_batch_golden(dec):
         assert np.abs(m - ref).max() < MEL_ABS_TOL
 
 
-def test_infer_fixture(dec):
+# The stage table of the reference's own verifier (tests/verify_flow.py:37-50):
+# (stage, golden key, shape of the capture); plus the 22 blocks.
+VERIFY_STAGES = (
+    ("spk", "spk", (1, 80)),
+    ("token_embed", "token_embed", (1, 12, 80)),
+    ("prelookahead", "prelookahead", (1, 12, 80)),
+    ("mu", "mu", (1, 80, 24)),
+    ("cond", "cond", (1, 80, 24)),
+    ("time_embed", "time_embed_step1", (2, 1024)),
+    ("input_proj", "dit_input_proj_step1", (2, 24, 1024)),
+    ("conv_pos", "dit_conv_pos_step1", (2, 24, 1024)),
+    ("input_embed", "dit_input_embed_step1", (2, 24, 1024)),
+    ("norm_out", "dit_norm_out_step1", (2, 24, 1024)),
+    ("dphi", "dphi_step1", (2, 80, 24)),
+)
+
+
+def test_infer_fixture(dec, weights):
     """Token-level infer (frontend + 10-step decode) on the reference's own
-    24-frame validation case, stage captures included."""
+    24-frame validation case: every stage of the reference's FlowDebug,
+    checked as its verifier checks it (rel = max|d| / max|ref| within the 1e-2
+    gate), against the golden vectors the reference produced; the 22 block
+    outputs against the golden where it holds them (blocks 0, 10, 21) and
+    against the oracle's step-1 captures for all 22."""
     g = golden("flow_fixture.npz")
     dbg = {}
     mel = dec.infer(g["prompt_tokens"][0], g["tokens"][0], g["prompt_feat"][0], g["spk_embedding"][0],
@@ -124,15 +145,25 @@ def test_infer_fixture(dec):
     assert mel is not None
     assert mel.shape == g["feat"][0].shape
     assert np.abs(mel - g["feat"][0]).max() < MEL_ABS_TOL
+    assert rel_max(mel, g["feat"][0]) < STAGE_TOL
+    for stage, key, shape in VERIFY_STAGES:
+        got = dbg[stage]
+        assert got.size == int(np.prod(shape)), stage
+        assert rel_max(got.reshape(shape), g[key]) < STAGE_TOL, stage
+    # the frontend runs in fp32 on both sides: much tighter than the gate
     assert rel_max(dbg["spk"], g["spk"][0]) < 1e-5
+    assert rel_max(dbg["token_embed"], g["token_embed"][0]) == 0.0
+    assert rel_max(dbg["prelookahead"], g["prelookahead"][0]) < 1e-5
     assert rel_max(dbg["mu"], g["mu"][0]) < 1e-5
     assert rel_max(dbg["cond"], g["cond"][0]) < 1e-6
-    assert rel_max(dbg["time_embed"], g["time_embed_step1"][0]) < 1e-5
-    assert rel_max(dbg["input_embed"], g["dit_input_embed_step1"]) < STAGE_TOL
+    assert rel_max(dbg["time_embed"], g["time_embed_step1"]) < 1e-5
     for i in (0, 10, 21):
         assert rel_max(dbg["blocks"][i], g[f"dit_block{i}"]) < STAGE_TOL
-    assert rel_max(dbg["norm_out"], g["dit_norm_out_step1"]) < STAGE_TOL
-    assert rel_max(dbg["dphi"], g["dphi_step1"]) < STAGE_TOL
+    cap = {}
+    fo.infer(weights, g["prompt_tokens"][0], g["tokens"][0], g["prompt_feat"][0], g["spk_embedding"][0],
+             g["noise_z"][0], capture=cap)
+    for i in range(22):
+        assert rel_max(dbg["blocks"][i], cap["blocks"][i]) < STAGE_TOL, i
 
 
 def test_decode_chunked_vs_oracle(dec, weights):

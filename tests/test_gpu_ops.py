@@ -11,7 +11,7 @@ import pytest
 
 torch = pytest.importorskip("torch")
 
-from conftest import rel_l2, rel_max  # noqa: E402
+from conftest import attn_ref_fp64, packed_starts, rel_l2, rel_max  # noqa: E402
 from oracle import flow_oracle as fo  # noqa: E402
 
 pytestmark = pytest.mark.gpu
@@ -44,32 +44,10 @@ def test_gemm(lib, M, N, K):
     assert err < 1e-5, err
 
 
-def _packed(lengths):
-    starts, r = [], 0
-    for L in lengths:
-        starts.append(r)
-        r += (L + 7) // 8 * 8
-    return starts, r
-
-
-def _attn_ref(q, k, v, lengths, starts, chunk):
-    out = np.zeros_like(q)
-    for L, s in zip(lengths, starts):
-        mask = fo.block_causal_mask([L], L, chunk)[0] if chunk else np.ones((L, L), bool)
-        qs, ks, vs = q[s:s + L], k[s:s + L], v[s:s + L]
-        for h in range(16):
-            sl = slice(64 * h, 64 * h + 64)
-            sc = (qs[:, sl] @ ks[:, sl].T) / 8.0
-            sc = np.where(mask, sc, -np.inf)
-            p = np.exp(sc - sc.max(-1, keepdims=True))
-            out[s:s + L, sl] = (p / p.sum(-1, keepdims=True)) @ vs[:, sl]
-    return out
-
-
 @pytest.mark.parametrize("lengths,chunk", [([1], 0), ([37], 0), ([128], 0), ([300, 129], 0), ([1000], 0),
                                            ([56, 306, 111], 50), ([556], 50), ([5, 200], 7)])
 def test_attention(lib, lengths, chunk):
-    starts, R = _packed(lengths)
+    starts, R = packed_starts(lengths)
     g = torch.Generator().manual_seed(sum(lengths) + chunk)
     q = (torch.randn(R, 1024, generator=g) * 1.5).to(torch.bfloat16)
     k = (torch.randn(R, 1024, generator=g) * 1.5).to(torch.bfloat16)
@@ -78,7 +56,7 @@ def test_attention(lib, lengths, chunk):
     qd, kd, vd = q.cuda(), k.cuda(), v.cuda()   # keep the device tensors alive across the call
     lib.op_attention(lengths, qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), out.data_ptr(), chunk)
     torch.cuda.synchronize()
-    ref = _attn_ref(q.double().numpy(), k.double().numpy(), v.double().numpy(), lengths, starts, chunk)
+    ref = attn_ref_fp64(q.double().numpy(), k.double().numpy(), v.double().numpy(), lengths, starts, chunk)
     got = out.float().cpu().numpy()
     rows = np.concatenate([np.arange(s, s + L) for s, L in zip(starts, lengths)])
     # the output is stored in bf16: compare against the bf16 rounding of the

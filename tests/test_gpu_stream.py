@@ -30,9 +30,14 @@ def dec(tmp_path_factory):
 def test_streaming_call_golden(dec):
     g = golden("flow_stream.npz")
     args = (g["prompt_tokens"][0], g["tokens"][0], g["prompt_feat"][0], g["spk_embedding"][0])
-    mel_s = dec.infer(*args, noise_z=g["noise_z"][0], finalize=False)
+    dbg_s = {}
+    mel_s = dec.infer(*args, noise_z=g["noise_z"][0], finalize=False, debug=dbg_s)
     assert mel_s is not None and mel_s.shape == g["feat_stream"][0].shape
     assert np.abs(mel_s - g["feat_stream"][0]).max() < MEL_ABS_TOL
+    # the streaming PreLookahead (last 3 tokens as context): 16 tokens in, 13 rows out
+    assert dbg_s["token_embed"].shape == (16, 80)
+    assert dbg_s["prelookahead"].shape == g["prelookahead"][0].shape
+    assert np.abs(dbg_s["prelookahead"] - g["prelookahead"][0]).max() < 1e-5 * np.abs(g["prelookahead"]).max()
     dbg = {}
     mel_f = dec.infer(*args, noise_z=g["noise_z"][0], finalize=True, debug=dbg)
     assert np.abs(mel_f - g["feat_final"][0]).max() < MEL_ABS_TOL
