@@ -227,6 +227,16 @@ int lx_flow_op_attention(int n_seq, const int32_t* lengths, const void* q, const
 int lx_flow_op_attention_static(int n_seq, const int32_t* lengths, const void* q, const void* k, const void* v,
                                 void* out, int chunk, void* stream);
 
+/* ---- failure-path self test (no reference counterpart) ------------------
+ * Runs one CTA whose consumer waits, through the library's bounded mbarrier
+ * wait, for a producer that arrives only if producer_arrives != 0, with a
+ * limit of limit_ms (0 < limit_ms <= 2000; the kernels themselves use 2 s).
+ * Returns LX_OK when the wait completed, LX_ERR_TIMEOUT when it ran out (the
+ * CTA then left through its abort flag and freed its tensor memory; the CUDA
+ * context stays usable).  *device_code (may be NULL) receives the raw device
+ * error code (0, or the role that gave up).  Synchronous on `stream`. */
+int lx_flow_selftest_wait(int producer_arrives, double limit_ms, int* device_code, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -88,20 +88,26 @@ constexpr uint32_t LX_WAIT_SUSPEND_NS = 1000000u;  // 1 ms per suspended try
 
 // Bounded wait for the phase of the given parity to complete.  Returns false
 // (after recording `code` in *err and raising *abort) when the wait exceeds
-// the timeout, or when another role of the CTA has already aborted.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, volatile int* abort_flag,
-                                          int code) {
+// `limit_ns`, or when another role of the CTA has already aborted.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, int* err, volatile int* abort_flag,
+                                              int code, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   for (;;) {
     if (mbar_try_wait_hint(bar, parity, LX_WAIT_SUSPEND_NS)) return true;
     if (*abort_flag) return false;
-    if (global_timer_ns() - t0 > LX_WAIT_TIMEOUT_NS) {
+    if (global_timer_ns() - t0 > limit_ns) {
       if (err) atomicCAS(err, 0, code);
       *abort_flag = 1;
       return false;
     }
   }
+}
+
+// The wait every kernel of the library uses: limit LX_WAIT_TIMEOUT_NS.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, volatile int* abort_flag,
+                                          int code) {
+  return mbar_wait_for(bar, parity, err, abort_flag, code, LX_WAIT_TIMEOUT_NS);
 }
 
 // ---------------------------------------------------------------------------

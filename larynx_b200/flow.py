@@ -32,7 +32,7 @@ EXPORTS = ("lx_flow_create", "lx_flow_destroy", "lx_flow_last_error", "lx_flow_l
            "lx_flow_infer", "lx_flow_decode", "lx_flow_decode_device", "lx_flow_estimator",
            "lx_flow_launch_count", "lx_flow_op", "lx_flow_op_gemm", "lx_flow_op_attention",
            "lx_flow_profile_decode", "lx_flow_op_attention_static", "lx_flow_infer_ex", "lx_flow_save_layout",
-           "lx_flow_load_layout")
+           "lx_flow_load_layout", "lx_flow_selftest_wait")
 
 PRE_LOOKAHEAD = 3  # PreLookaheadLayer look-ahead tokens (cosyvoice3.yaml pre_lookahead_len)
 
@@ -97,7 +97,8 @@ def load_library(path: str = LIB_PATH):
     lib.lx_flow_op_gemm.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int, vp, vp, vp, vp, vp]
     lib.lx_flow_op_attention.argtypes = [ctypes.c_int, _i32p, vp, vp, vp, vp, ctypes.c_int, vp]
     lib.lx_flow_op_attention_static.argtypes = [ctypes.c_int, _i32p, vp, vp, vp, vp, ctypes.c_int, vp]
-    for name in ("lx_flow_op_gemm", "lx_flow_op_attention", "lx_flow_op_attention_static", "lx_flow_infer_ex",
+    lib.lx_flow_selftest_wait.argtypes = [ctypes.c_int, ctypes.c_double, ctypes.POINTER(ctypes.c_int), vp]
+    for name in ("lx_flow_selftest_wait", "lx_flow_op_gemm", "lx_flow_op_attention", "lx_flow_op_attention_static", "lx_flow_infer_ex",
                  "lx_flow_save_layout", "lx_flow_load_layout", "lx_flow_create", "lx_flow_load_gguf", "lx_flow_load_noise", "lx_flow_infer", "lx_flow_decode",
                  "lx_flow_decode_device", "lx_flow_estimator", "lx_flow_op"):
         getattr(lib, name).restype = ctypes.c_int
@@ -331,3 +332,14 @@ def op_attention_static(lengths, q_ptr: int, k_ptr: int, v_ptr: int, out_ptr: in
                                          v(out_ptr), int(chunk), v(stream))
     if rc != LX_OK:
         raise FlowError(f"lx_flow_op_attention_static failed: {ERRORS.get(rc, rc)}")
+
+
+def selftest_wait(producer_arrives: bool, limit_ms: float, stream: int = 0):
+    """Run the bounded-wait self test (lx_flow_selftest_wait): returns
+    (status, device error code).  status is LX_OK when the producer arrived
+    and 7 (LX_ERR_TIMEOUT) when the wait ran out after ``limit_ms``."""
+    lib = load_library()
+    code = ctypes.c_int(-1)
+    rc = lib.lx_flow_selftest_wait(int(bool(producer_arrives)), float(limit_ms), ctypes.byref(code),
+                                   ctypes.c_void_p(stream or None))
+    return rc, code.value

@@ -77,8 +77,18 @@ def _conv1d_s1_f64(x: np.ndarray, W: np.ndarray, b: np.ndarray, pad_left: int) -
     return acc
 
 
+_libm_exp = np.frompyfunc(math.exp, 1, 1)
+
+
 def _elu(v: np.ndarray) -> np.ndarray:
-    return np.where(v <= 0.0, np.exp(np.minimum(v, 0.0)) - 1.0, v)
+    """source.cpp:38-40: x <= 0 -> std::exp(x) - 1.  The exponential is the C
+    library's (Python's math.exp): numpy's vectorised float64 exp differs from
+    it in the last bit for some inputs, which the reference's own compiled
+    source.cpp (oracle/_ref) shows."""
+    out = np.array(v, np.float64, copy=True)
+    neg = out <= 0.0
+    out[neg] = _libm_exp(out[neg]).astype(np.float64) - 1.0
+    return out
 
 
 def f0_predict(mel: np.ndarray, w: Dict[str, np.ndarray]) -> np.ndarray:

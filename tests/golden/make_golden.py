@@ -2,8 +2,8 @@
 """Generate the golden fixtures under tests/golden/ from the reference itself.
 
 Imports hardenedlinux/larynx's own ground-truth Flow model,
-``tests/flow_reference.py`` (path from $LARYNX_REF, default: the read-only
-reference checkout), loads the seeded synthetic weights of
+``tests/flow_reference.py`` (from the reference checkout named by
+$LARYNX_REF, which is required), loads the seeded synthetic weights of
 ``oracle.flow_oracle.synth_weights`` (seed 0, N(0, 0.02); the rotary
 ``inv_freq`` buffer keeps its formula value) and records:
 
@@ -26,7 +26,7 @@ reference checkout), loads the seeded synthetic weights of
                     chunks for the 10-step schedule)
 
 Run once in a container where the reference is readable:
-    python tests/golden/make_golden.py
+    LARYNX_REF=<reference checkout> python tests/golden/make_golden.py
 The GPU box never runs this script; it only reads the .npz files.
 """
 
@@ -41,7 +41,9 @@ REPO = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, REPO)
 from oracle import flow_oracle as fo  # noqa: E402
 
-REF = os.environ.get("LARYNX_REF", "/root/reference")
+REF = os.environ.get("LARYNX_REF")
+if not REF:
+    sys.exit("set LARYNX_REF to the reference checkout (the folder holding tests/flow_reference.py)")
 sys.path.insert(0, os.path.join(REF, "tests"))
 import flow_reference as fr  # noqa: E402
 

@@ -193,3 +193,59 @@ def test_errors_are_reported(dec, tmp_path):
     d.close()
     with pytest.raises(Exception):
         dec.decode([0], np.zeros(0), np.zeros(0), np.zeros((1, 80)), noise=np.zeros(0))
+
+
+def test_noise_bank_production_path(dec, tmp_path):
+    """The 6-argument FlowDecoder::infer (flow.h:72-77, flow.cpp:290-308): the
+    CFM noise is the first MEL_T columns of the bank given to load_noise
+    (FNSE asset, flow.cpp:70-108).  It must equal the 7-argument call fed
+    that slice, bit for bit; so must the batched decode with noise=None."""
+    import struct
+
+    from larynx_b200.gguf import write_noise_bank
+    rng = np.random.default_rng(21)
+    bank = rng.standard_normal((80, 15000), dtype=np.float32)
+    path = str(tmp_path / "flow_noise.bin")
+    write_noise_bank(path, bank)
+    assert dec.load_noise(path), dec.last_error
+    g = golden("flow_fixture.npz")
+    args = (g["prompt_tokens"][0], g["tokens"][0], g["prompt_feat"][0], g["spk_embedding"][0])
+    T = 2 * (g["prompt_tokens"].size + g["tokens"].size)
+    a = dec.infer(*args)                                  # bank slice
+    b = dec.infer(*args, noise_z=bank[:, :T])             # explicit noise
+    assert a is not None and b is not None
+    np.testing.assert_array_equal(a, b)
+    # batched decode: noise=None slices the bank per utterance
+    L = [40, 17]
+    mus = [rng.standard_normal((80, n)).astype(np.float32) for n in L]
+    conds = [np.zeros((80, n), np.float32) for n in L]
+    spks = rng.standard_normal((2, 80)).astype(np.float32)
+    d0 = dec.decode(L, mus, conds, spks, noise=None)
+    d1 = dec.decode(L, mus, conds, spks, noise=[bank[:, :n] for n in L])
+    np.testing.assert_array_equal(d0, d1)
+
+    # idempotent like the reference (flow.cpp:72): a loaded bank stays loaded
+    assert dec.load_noise(str(tmp_path / "missing.bin"))
+    np.testing.assert_array_equal(dec.infer(*args), a)
+
+    # malformed assets are rejected with a status, on a handle with no bank yet
+    from larynx_b200 import FlowDecoder
+    fresh = FlowDecoder(0)
+
+    def bad(name, header, payload_floats):
+        p = str(tmp_path / name)
+        with open(p, "wb") as f:
+            f.write(header)
+            f.write(np.zeros(payload_floats, np.float32).tobytes())
+        return p
+    n = 80 * 15000
+    for p in (bad("magic.bin", struct.pack("<IIIQ", 0x12345678, 1, 80, 15000), n),
+              bad("version.bin", struct.pack("<IIIQ", 0x45534E46, 2, 80, 15000), n),
+              bad("mel.bin", struct.pack("<IIIQ", 0x45534E46, 1, 81, 15000), n),
+              bad("frames.bin", struct.pack("<IIIQ", 0x45534E46, 1, 80, 14999), n),
+              bad("short.bin", struct.pack("<IIIQ", 0x45534E46, 1, 80, 15000), n - 1),
+              str(tmp_path / "missing.bin")):
+        assert not fresh.load_noise(p), p
+        assert fresh.last_error
+    assert fresh.load_noise(path), fresh.last_error
+    fresh.close()
