@@ -9,18 +9,25 @@ Euler solver with CFG pairing (batch 2 per utterance) through the 22-block
 DiT, key-padding semantics (utterances packed without padding).  Weights are
 seeded random N(0, 0.02) of the real architecture (no checkpoint offline).
 
-One step = one full 10-step CFG decode of the rank's 64-utterance batch.
-`value` = mel frames decoded by all ranks / max-over-ranks device time, with
-inputs resident in HBM (lx_flow_decode_device); `e2e` = the same through the
-host-buffer C-ABI call lx_flow_decode (pinned inputs, H2D + compute + D2H of
-the mel every step).  Weak scaling: every rank decodes its own batch; there is
-no collective on the data path (barriers and the timing max only).
+One step = one full 10-step CFG decode of the 64-utterance set.  At N GPUs
+the set is split across the ranks by decode cost (larynx_b200.shard: LPT over
+a device-time model, then a local search), each rank decodes its shard, and
+`value` = the set's mel frames / max-over-ranks device time (strong scaling:
+the work is fixed as N grows), with inputs resident in HBM
+(lx_flow_decode_device); `e2e` = the same through the host-buffer C-ABI call
+lx_flow_decode (pinned inputs, H2D + compute + D2H of the mel every step).
+There is no collective on the data path (barriers and the timing max only).
+`cfg3_weak` (N > 1) is the weak-scaling view: every rank decodes the whole
+set.
 
 `--impl reference` times the reference's CPU path on the host cores.  The
 reference's own CPU engine (GGML, LARYNX_BACKEND=cpu) cannot be built (ggml is
 an un-vendored submodule), so the numpy restatement of the reference's Flow
 model (oracle/, checked against the reference's golden vectors) runs in its
-place, on a bounded sample of the workload per step.
+place on every host core, one Euler step of one config-3 utterance per step
+(a 10-step decode is ten such forwards, so frames / (10 x step time) is its
+throughput), the utterances taken from the set in a fixed order that mixes
+short and long ones.
 """
 
 import argparse
@@ -41,7 +48,7 @@ sys.path.insert(0, REPO)
 METRIC = "Flow mel-frames/s (10-step CFG)"
 UNIT = "mel-frames/s"
 N_UTT = 64
-REF_SAMPLE_T = 200
+REF_SAMPLE_STRIDE = 23   # coprime to 64: any run of steps visits lengths from the whole range
 
 
 def cfg3_lengths(n=N_UTT):
@@ -65,13 +72,22 @@ def cfg3_inputs(lengths, seed):
     return mu, cond, spks, noise
 
 
+def subset(lengths, arrays, idx):
+    """The utterances `idx` of a set laid out as concat_u [80][T_u] (mu, cond,
+    noise) and [U][80] (spks)."""
+    off = np.concatenate([[0], np.cumsum(np.asarray(lengths, np.int64) * 80)])
+    mu, cond, spks, noise = arrays
+    cat = lambda a: np.ascontiguousarray(np.concatenate([a[off[i]:off[i + 1]] for i in idx]))
+    return np.asarray(lengths)[idx], (cat(mu), cat(cond), np.ascontiguousarray(spks[idx]), cat(noise))
+
+
 def config_block(n_gpus, lengths):
-    return {"workload": f"cfg3: {len(lengths)} utterances per GPU, T~U[100,1500] frames (seed 3), "
+    return {"workload": f"cfg3: one set of {len(lengths)} utterances, T~U[100,1500] frames (seed 3), "
                         "10-step cosine CFM Euler, CFG batch 2, key-padding (packed varlen), dim 1024 x 22 blocks",
             "model": "CosyVoice3 Flow DiT (22 blocks, dim 1024, 16 heads x 64, FF 2048)",
-            "global_batch": int(len(lengths) * n_gpus), "seq_len": "100-1500 frames",
-            "frames_per_gpu": int(np.sum(lengths)),
-            "parallelism": f"dp{n_gpus} (independent utterance batches, no collectives)",
+            "global_batch": int(len(lengths)), "seq_len": "100-1500 frames",
+            "frames": int(np.sum(lengths)),
+            "parallelism": f"dp{n_gpus} (the set sharded across GPUs by decode cost, no collectives)",
             "l2": "inputs larger than L2 (bf16 weights 378 MB + >1 GB activations per step)"}
 
 
@@ -167,16 +183,20 @@ def load_traffic():
 # ---------------------------------------------------------------------------
 # CPU arms (the reference's algorithm restated in numpy: oracle/)
 # ---------------------------------------------------------------------------
-def cpu_sample_decode(W, T, seed):
+def cpu_euler_step(W, T, seed):
+    """One CFG Euler step (the DiT on the [cond; uncond] rows) of a T-frame
+    utterance, numpy oracle; returns its wall time."""
     from oracle import flow_oracle as fo
     rng = np.random.default_rng(seed)
+    x = rng.standard_normal((1, 80, T), dtype=np.float32)
     mu = rng.standard_normal((1, 80, T), dtype=np.float32)
-    z = rng.standard_normal((1, 80, T), dtype=np.float32)
     spk = rng.standard_normal((1, 80), dtype=np.float32)
     cond = np.zeros((1, 80, T), np.float32)
     cond[:, :, :int(0.2 * T)] = rng.standard_normal((1, 80, int(0.2 * T)), dtype=np.float32)
+    z = np.zeros_like(mu)
     t0 = time.perf_counter()
-    fo.solve_euler(W, z, mu, spk, cond)
+    fo.dit_forward(W, np.concatenate([x, x]), np.concatenate([mu, z]), np.full(2, 0.3, np.float32),
+                   np.concatenate([spk, np.zeros_like(spk)]), np.concatenate([cond, np.zeros_like(cond)]))
     return time.perf_counter() - t0
 
 
@@ -187,25 +207,51 @@ def cpu_cores():
         return os.cpu_count() or 1
 
 
+def cpu_sample(W, n, first):
+    """`n` samples from the config-3 set: one Euler step of utterance
+    order[(first + i) % 64] each.  Returns (frames / s of the 10-step decode,
+    the lengths visited)."""
+    lengths = np.sort(cfg3_lengths())
+    visit = [int(lengths[((first + i) * REF_SAMPLE_STRIDE) % len(lengths)]) for i in range(n)]
+    secs = [cpu_euler_step(W, T, 1000 + first + i) for i, T in enumerate(visit)]
+    return float(np.sum(visit)) / (10.0 * float(np.sum(secs))), visit
+
+
+def cpu_threads():
+    """Give numpy's BLAS every host core (torchrun sets OMP_NUM_THREADS=1)."""
+    n = cpu_cores()
+    try:
+        from threadpoolctl import threadpool_limits
+        threadpool_limits(limits=n)
+    except Exception:
+        pass
+    return n
+
+
+CPU_SAMPLE_ABOUT = ("one CFG Euler step (DiT forward on the cond + uncond rows) of one config-3 utterance per "
+                    "sample, utterances from the 64-utterance set in a fixed order mixing short and long ones; "
+                    "frames / (10 x time), a 10-step decode being ten such forwards; numpy fp32 restatement of "
+                    "the reference's Flow model (oracle/) on every host core; the reference's GGML CPU engine "
+                    "is unavailable (ggml submodule not vendored)")
+
+
 def run_reference(args):
     """The reference arm: rank 0 only; other ranks exit without work."""
     if int(os.environ.get("RANK", "0")) != 0:
         return
     from oracle import flow_oracle as fo
+    cores = cpu_threads()
     W = fo.synth_weights(seed=0, std=0.02)
-    for i in range(args.warmup):
-        cpu_sample_decode(W, REF_SAMPLE_T, 100 + i)
-    times = [cpu_sample_decode(W, REF_SAMPLE_T, 1000 + i) for i in range(args.steps)]
-    tot = float(np.sum(times))
-    value = args.steps * REF_SAMPLE_T / tot
-    sample = (f"1 utterance x {REF_SAMPLE_T} frames per step (cfg3 input distribution), full 10-step CFG decode, "
-              "numpy fp32 restatement of the reference's Flow model (oracle/); the reference's GGML CPU engine "
-              "is unavailable (ggml submodule not vendored)")
+    cpu_sample(W, args.warmup, 64)
+    t0 = time.perf_counter()
+    value, visit = cpu_sample(W, args.steps, 0)
+    wall = time.perf_counter() - t0
+    sample = f"{CPU_SAMPLE_ABOUT}; {args.steps} samples, {int(np.sum(visit))} frames"
     line = {"metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": tot / args.steps * 1e3,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": wall / args.steps * 1e3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": config_block(args.gpus, cfg3_lengths()),
-            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cpu_cores(), "kind": "port", "sample": sample},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -420,9 +466,17 @@ def run_ours(args):
     if not dec.load(gguf):
         raise SystemExit(f"load failed: {dec.last_error}")
 
-    lengths = cfg3_lengths(args.utts)
+    # the config-3 set; this rank decodes its shard (the whole set at N = 1)
+    all_lengths = cfg3_lengths(args.utts)
+    all_arrays = cfg3_inputs(all_lengths, seed=3000)
+    total_frames = int(all_lengths.sum())
+    if dist_on:
+        from larynx_b200 import shard
+        mine = shard.lpt_partition(all_lengths, world)[rank]
+    else:
+        mine = np.arange(len(all_lengths))
+    lengths, (mu, cond, spks, noise) = subset(all_lengths, all_arrays, mine)
     tot = int(lengths.sum())
-    mu, cond, spks, noise = cfg3_inputs(lengths, seed=3000 + rank)
     dev = torch.device("cuda", local)
     d_mu = torch.from_numpy(mu).to(dev)
     d_cond = torch.from_numpy(cond).to(dev)
@@ -454,7 +508,8 @@ def run_ours(args):
         barrier()
         launches = dec.launch_count - n0
         clk = clocks.stop() if rank == 0 else None
-        ms = max_over_ranks(e0.elapsed_time(e1))
+        local_ms = e0.elapsed_time(e1)
+        ms = max_over_ranks(local_ms)
     finite = bool(torch.isfinite(d_out).all().item())
 
     # e2e through the host-buffer C-ABI call, pinned inputs and output
@@ -476,9 +531,10 @@ def run_ours(args):
             e2e_step()
         barrier()
         e2e_s = max_over_ranks(time.perf_counter() - t0)
-        e2e = {"value": world * tot * args.steps / e2e_s, "unit": UNIT,
+        e2e = {"value": total_frames * args.steps / e2e_s, "unit": UNIT,
                "h2d_bytes_per_step": int(mu.nbytes + cond.nbytes + spks.nbytes + noise.nbytes),
                "d2h_bytes_per_step": int(tot * 80 * 4), "ms_per_step": e2e_s / args.steps * 1e3,
+               "bytes_note": "per rank (this rank's shard)" if dist_on else "whole set",
                "api": "lx_flow_decode (host buffers)"}
 
     # per-kernel-class device times (CUDA events around every launch, no graph)
@@ -554,14 +610,10 @@ def run_ours(args):
         extra["cfg2_frames_per_s"] = 1000.0 / (float(np.median(times)) * 1e-3)
 
     if dist_on:
-        # strong-scaling view of config 3: the one 64-utterance set split across
-        # the ranks by LPT over the decode cost (larynx_b200.shard)
-        from larynx_b200 import shard
-        mine = shard.lpt_partition(lengths, world)[rank]
-        Ls = lengths[mine]
-        ms_, cs_, ss_, ns_ = cfg3_inputs(Ls, seed=3000)
-        ts_ = [torch.from_numpy(a).to(dev) for a in (ms_, cs_, ss_, ns_)]
-        os_ = torch.empty_like(ts_[0])
+        # weak-scaling view: every rank decodes the whole 64-utterance set
+        wl, wa = all_lengths, all_arrays
+        tw = [torch.from_numpy(a).to(dev) for a in wa]
+        ow = torch.empty_like(tw[0])
         with torch.cuda.stream(stream):
             for i in range(3):
                 if i == 2:
@@ -569,14 +621,23 @@ def run_ours(args):
                     b0 = torch.cuda.Event(enable_timing=True)
                     b1 = torch.cuda.Event(enable_timing=True)
                     b0.record(stream)
-                dec.decode_device(Ls, ts_[0].data_ptr(), ts_[1].data_ptr(), ts_[2].data_ptr(), ts_[3].data_ptr(),
-                                  os_.data_ptr(), stream=stream.cuda_stream)
+                dec.decode_device(wl, tw[0].data_ptr(), tw[1].data_ptr(), tw[2].data_ptr(), tw[3].data_ptr(),
+                                  ow.data_ptr(), stream=stream.cuda_stream)
             b1.record(stream)
             stream.synchronize()
-        sms = max_over_ranks(b0.elapsed_time(b1))
-        extra["cfg3_lpt_strong"] = {"value": float(lengths.sum()) / (sms * 1e-3), "unit": UNIT,
-                                    "ms": sms, "utterances_this_rank": int(len(mine)),
-                                    "about": "the 64-utterance set LPT-sharded across ranks (strong scaling)"}
+        wms = max_over_ranks(b0.elapsed_time(b1))
+        extra["cfg3_weak"] = {"value": world * float(total_frames) / (wms * 1e-3), "unit": UNIT, "ms": wms,
+                              "about": "every rank decodes the whole 64-utterance set (weak scaling)"}
+        del tw, ow
+        per_rank = torch.zeros(world, 2, dtype=torch.float64, device=dev)
+        per_rank[rank, 0] = local_ms / args.steps
+        per_rank[rank, 1] = tot
+        dist.all_reduce(per_rank)
+        pr = per_rank.cpu().numpy()
+        extra["shards"] = {"ms_per_step_by_rank": [round(float(v), 2) for v in pr[:, 0]],
+                           "frames_by_rank": [int(v) for v in pr[:, 1]],
+                           "balance_max_over_mean": float(pr[:, 0].max() / pr[:, 0].mean()),
+                           "partition": "larynx_b200.shard.lpt_partition (LPT + local search on a device-time model)"}
     if not args.no_cfg1:
         extra["cfg1_ops"] = bench_cfg1(dev, stream)
     if not args.no_cfg4:
@@ -587,20 +648,20 @@ def run_ours(args):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         from oracle import flow_oracle as fo
+        cores = cpu_threads()
         W = fo.synth_weights(seed=0, std=0.02)
-        cpu_sample_decode(W, 48, 7)  # warm the BLAS threads
-        ts = [cpu_sample_decode(W, REF_SAMPLE_T, 1000 + i) for i in range(2)]
-        cpu = {"value": REF_SAMPLE_T * len(ts) / float(np.sum(ts)), "unit": UNIT, "cores": cpu_cores(),
-               "kind": "port",
-               "sample": f"1 utterance x {REF_SAMPLE_T} frames (cfg3 input distribution), 10-step CFG decode, "
-                         f"x{len(ts)}; numpy fp32 restatement of the reference's Flow model (oracle/)"}
+        cpu_euler_step(W, 48, 7)  # warm the BLAS threads
+        v, visit = cpu_sample(W, 3, 0)
+        cpu = {"value": v, "unit": UNIT, "cores": cores, "kind": "port",
+               "sample": f"{CPU_SAMPLE_ABOUT}; {len(visit)} samples, {int(np.sum(visit))} frames"}
 
     if rank == 0:
-        value = world * tot * args.steps / (ms * 1e-3)
+        value = total_frames * args.steps / (ms * 1e-3)
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-                "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+                "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded random weights and inputs)",
-                "config": config_block(world, lengths), "rtf": (ms / args.steps * 1e-3) / (tot / 50.0),
+                "config": config_block(world, all_lengths),
+                "rtf": (ms / args.steps * 1e-3) / (total_frames / 50.0),
                 "e2e": e2e, "gpu_launches": int(launches), "roofline": roofline, "cpu_baseline": cpu,
                 "clocks": clk, "kernels": breakdown, "attention": attn, "finite": finite, **extra}
         sys.stdout.flush()

@@ -2,16 +2,25 @@
 
 Utterances of a batch share nothing on the Flow hot path (the Euler loop has
 no cross-utterance term), so N GPUs decode N disjoint shards with no
-collective on the data path.  The shards are balanced by the decode cost of an
-utterance of T frames, which is linear in T for the projections and quadratic
-for attention:
+collective on the data path.  The shards are balanced by a device-time model
+of the 10-step CFG decode of an utterance of T frames, fitted to the
+per-kernel times of the whole config-3 decode on one B200 (CUDA events around
+every launch, lx_flow_profile_decode):
 
-    c(T) = T * 378.04e6 + T^2 * 90112      (FLOPs per CFG row, one DiT forward)
+    c(T) = T * LINEAR_MS_PER_FRAME + ceil(T / 128) * 128 * T * ATTN_MS_PER_PAIR
 
-(378.04 MFLOP per token: input projection, conv-pos, 22 x (QKV, out, FFN),
-proj_out; 90112 = 4 * 1024 * 22 attention FLOP per token pair.)  The
-partition is greedy longest-processing-time first: utterances in decreasing
-cost, each to the currently lightest rank.
+The linear term is everything whose work grows with the frame count (the
+projection GEMMs, conv-pos, AdaLN, the Euler update: 382 ms for the 47,726
+frames of the config-3 set); the quadratic term is attention, whose work is
+its 128-row query tiles times the keys they see (200.8 ms for 49.3 M
+tile-row x key pairs).  Attention runs at a lower fraction of the tensor
+peak than the GEMMs, so a FLOP count (378 MFLOP per frame + 90 kFLOP per
+frame pair) under-weights long utterances.
+
+The partition is greedy longest-processing-time first (utterances in
+decreasing cost, each to the currently lightest rank), followed by a local
+search that moves or swaps single utterances out of the most loaded rank
+while that lowers the maximum load.
 
 `gather_to_rank0` reassembles per-utterance results in the caller's original
 order on rank 0 through torch.distributed (gloo on the host, NCCL on GPUs).
@@ -23,14 +32,54 @@ from typing import List, Sequence
 
 import numpy as np
 
-FLOP_PER_TOKEN = 378.04e6
-FLOP_PER_TOKEN_PAIR = 4 * 1024 * 22
+LINEAR_MS_PER_FRAME = 8.006e-3
+ATTN_MS_PER_PAIR = 4.071e-6
+ATT_Q_TILE = 128
 
 
 def utterance_cost(T) -> np.ndarray:
-    """Decode cost (FLOPs per CFG row per DiT forward) of utterances of T frames."""
+    """Modelled device time (ms) of the 10-step CFG decode of utterances of T frames."""
     T = np.asarray(T, dtype=np.float64)
-    return T * FLOP_PER_TOKEN + T * T * FLOP_PER_TOKEN_PAIR
+    q = np.ceil(T / ATT_Q_TILE) * ATT_Q_TILE
+    return T * LINEAR_MS_PER_FRAME + q * T * ATTN_MS_PER_PAIR
+
+
+def _refine(cost: np.ndarray, parts: List[list], max_rounds: int = 1000) -> None:
+    """Move or swap one utterance at a time between the most loaded rank and
+    another while the maximum load falls."""
+    n = len(parts)
+    load = np.array([cost[p].sum() for p in parts])
+    for _ in range(max_rounds):
+        hi = int(np.argmax(load))
+        best = (load[hi], None)
+        for lo in range(n):
+            if lo == hi:
+                continue
+            for a in parts[hi]:
+                # move a: hi -> lo
+                m = max(load[hi] - cost[a], load[lo] + cost[a])
+                if m < best[0] - 1e-12:
+                    best = (m, (lo, a, None))
+                for b in parts[lo]:
+                    d = cost[a] - cost[b]
+                    if d <= 0:
+                        continue
+                    m = max(load[hi] - d, load[lo] + d)
+                    if m < best[0] - 1e-12:
+                        best = (m, (lo, a, b))
+        if best[1] is None:
+            return
+        lo, a, b = best[1]
+        parts[hi].remove(a)
+        parts[lo].append(a)
+        load[hi] -= cost[a]
+        load[lo] += cost[a]
+        if b is not None:
+            parts[lo].remove(b)
+            parts[hi].append(b)
+            load[lo] -= cost[b]
+            load[hi] += cost[b]
+        # the old maximum fell; a rank other than `hi` may now be the maximum
 
 
 def lpt_partition(lengths: Sequence[int], n_ranks: int) -> List[np.ndarray]:
@@ -46,6 +95,7 @@ def lpt_partition(lengths: Sequence[int], n_ranks: int) -> List[np.ndarray]:
         r = int(np.argmin(load))
         parts[r].append(int(i))
         load[r] += cost[i]
+    _refine(cost, parts)
     return [np.array(sorted(p), dtype=np.int64) for p in parts]
 
 

@@ -79,3 +79,25 @@ def test_gather_two_gloo_ranks():
         assert p.exitcode == 0
     res = [q.get(timeout=10) for _ in range(2)]
     assert all(res)
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_refined_partition_is_near_perfect_on_cfg3(world):
+    """LPT + local search on the device-time model: the most loaded rank is
+    within 0.5% of the mean on the config-3 set, never worse than plain LPT."""
+    L = _cfg3()
+    parts = shard.lpt_partition(L, world)
+    loads = shard.shard_loads(L, parts)
+    assert loads.max() / loads.mean() < 1.005
+    cost = shard.utterance_cost(L)
+    plain = np.zeros(world)
+    for i in np.argsort(-cost, kind="stable"):
+        plain[int(np.argmin(plain))] += cost[i]
+    assert loads.max() <= plain.max() + 1e-9
+
+
+def test_cost_model_weights_attention_by_query_tiles():
+    # 128 and 129 frames: the second needs a second 128-row query tile
+    c = shard.utterance_cost([128, 129])
+    lin = shard.LINEAR_MS_PER_FRAME
+    assert c[1] - c[0] > lin + 128 * 128 * shard.ATTN_MS_PER_PAIR
