@@ -39,41 +39,20 @@ namespace lx {
 
 namespace {
 
-// Softmax warpgroups per CTA (NWG): 1 -- one thread per query row over all
-// 128 keys of a tile; 2 -- two threads per row, each over one 64-key half
-// (twice the softmax warps per SM sub-partition to hide the latency of the
-// exponential chains; the halves share the row's reference maximum through
-// shared memory once per tile and their row sums once per item).
-// Register split with setmaxnreg: two blocks per SM; warpgroup 0 (TMA, MMA)
-// drops to PRODUCER registers, the softmax warpgroups rise to SOFTMAX.
-// attention() checks the launch register count before the first launch, so
-// the raise can always be met.
-template <int NWG>
-struct AttShape;
-template <>
-struct AttShape<1> {  // 256 x 128 = 32768 = 128 x 48 + 128 x 208
-  static constexpr int THREADS = 256, LAUNCH_REGS = 128, PRODUCER = 48, SOFTMAX = 208;
-};
-template <>
-struct AttShape<2> {  // 384 x 80 = 30720 = 128 x 32 + 256 x 104
-  static constexpr int THREADS = 384, LAUNCH_REGS = 80, PRODUCER = 32, SOFTMAX = 104;
-};
-static_assert(128 * AttShape<1>::PRODUCER + 128 * AttShape<1>::SOFTMAX <=
-                  AttShape<1>::THREADS * AttShape<1>::LAUNCH_REGS, "register split");
-static_assert(128 * AttShape<2>::PRODUCER + 256 * AttShape<2>::SOFTMAX <=
-                  AttShape<2>::THREADS * AttShape<2>::LAUNCH_REGS, "register split");
-static_assert(AttShape<2>::THREADS * AttShape<2>::LAUNCH_REGS * 2 <= 65536, "two blocks per SM");
+constexpr int ATT_THREADS = 256;  // warpgroup 0: K TMA, MMA, V TMA, idle; warpgroup 1: softmax
+// Register split with setmaxnreg: the block is launched with 256 x 128 = 32768
+// registers (two blocks per SM); warpgroup 0 drops to 48, warpgroup 1 rises
+// to 208: 128 x 48 + 128 x 208 = 32768.  attention() checks the launch
+// register count before the first launch, so the raise can always be met.
+constexpr int ATT_LAUNCH_REGS = 128;
+constexpr int REGS_PRODUCER = 48;
+constexpr int REGS_SOFTMAX = 208;
+static_assert(128 * REGS_PRODUCER + 128 * REGS_SOFTMAX <= ATT_THREADS * ATT_LAUNCH_REGS, "register split");
 constexpr int ATT_STAGES = 2;
 constexpr int Q_BYTES = 128 * 64 * 2;  // 16 KB
 constexpr int K_BYTES = 128 * 64 * 2;  // 16 KB
 constexpr int V_BYTES = 128 * 64 * 2;  // 16 KB: 128 keys x 64 fp16 values (MN-major B of PV)
-// NWG = 2 exchange area: half-row maxima [2 tiles][2 halves][128 rows], row
-// sums [2 halves][128 rows], and 12 mbarriers (4 lane quarters x (2 + 1))
-constexpr int XCH_BYTES = (2 * 2 * 128 + 2 * 128) * 4 + 12 * 8;
-template <int NWG>
-constexpr int att_smem_bytes() {
-  return 1024 + 2 * Q_BYTES + ATT_STAGES * (K_BYTES + V_BYTES) + 256 + (NWG == 2 ? XCH_BYTES : 0);
-}
+constexpr int ATT_SMEM = 1024 + 2 * Q_BYTES + ATT_STAGES * (K_BYTES + V_BYTES) + 256;
 constexpr uint32_t ATT_TMEM_COLS = 256;
 constexpr uint32_t S_COL = 0, P_COL = 128, O_COL = 192;
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units: P <= 2^8
@@ -211,237 +190,7 @@ __device__ __forceinline__ AttnItem load_item(const AttnTile* __restrict__ tiles
   return it;
 }
 
-__device__ __forceinline__ void tmem_st8u(uint32_t taddr, const uint32_t (&v)[8]) {
-  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(v[0]),
-               "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
-               : "memory");
-}
-
-// p = 2^(s * sl2 - m) for 16 scores, their sum added to acc, packed as 8 fp16 pairs.
-__device__ __forceinline__ void exp_chunk16(const float* s, float sl2, float m, float2& acc0, float2& acc1,
-                                            uint32_t* pk) {
-  const float2 scale = make_float2(sl2, sl2);
-  const float2 neg_m = make_float2(-m, -m);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const float2 x = __ffma2_rn(make_float2(s[2 * i], s[2 * i + 1]), scale, neg_m);
-    const float2 p = make_float2(ex2(x.x), ex2(x.y));
-    if (i & 1)
-      acc1 = __fadd2_rn(acc1, p);
-    else
-      acc0 = __fadd2_rn(acc0, p);
-    pk[i] = pack_f16x2(p.x, p.y);
-  }
-}
-
-__device__ __forceinline__ void tmem_st16u(uint32_t taddr, const uint32_t (&v)[16]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
-      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
-      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
-      "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
-      : "memory");
-}
-
-// Shared-memory layout of the barrier area (offsets from `bars`).
-static_assert(ATT_STAGES == 2, "barrier offsets below assume two ring stages");
-constexpr uint32_t OFF_S_FULL = 96, OFF_S_EMPTY = 104, OFF_P_FULL = 112, OFF_O_DONE = 120, OFF_O_FREE = 128;
-constexpr uint32_t OFF_ABORT = 140;                 // tmem_slot at 136
-constexpr uint32_t OFF_XMAX = 256;                  // float [2 buffers][2 halves][128 rows]
-constexpr uint32_t OFF_XSUM = OFF_XMAX + 2048;      // float [2 halves][128 rows]
-constexpr uint32_t OFF_XBAR = OFF_XSUM + 1024;      // mbarrier [4 quarters][2 buffers]
-constexpr uint32_t OFF_LBAR = OFF_XBAR + 64;        // mbarrier [4 quarters]
-static_assert(OFF_LBAR + 32 - OFF_XMAX <= XCH_BYTES, "exchange area");
-
-__device__ __forceinline__ void st_shared_f32(uint32_t a, float v) {
-  asm volatile("st.shared.f32 [%0], %1;" ::"r"(a), "f"(v) : "memory");
-}
-__device__ __forceinline__ float ld_shared_f32(uint32_t a) {
-  float v;
-  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a) : "memory");
-  return v;
-}
-
-// Both warps of a lane quarter arrive on `bar` (lane 0 of each, after the
-// warp's shared-memory writes) and wait for its phase `parity` (bounded).
-__device__ __forceinline__ bool pair_sync(uint32_t bar, uint32_t parity, int* err, uint32_t abort_a) {
-  __syncwarp();
-  if ((threadIdx.x & 31) == 0) mbar_arrive_a(bar);
-  const bool ok = mbar_wait_a(bar, parity, err, abort_a, DEV_TIMEOUT_SOFTMAX);
-  return __all_sync(0xffffffffu, ok);
-}
-
-// Softmax of the NWG = 2 layout: warps 4..7 take keys [0, 64) of every tile,
-// warps 8..11 keys [64, 128), thread = (query row, key half).  The two
-// halves of a row keep one reference maximum: each tile they exchange their
-// half maxima through shared memory (two buffers, alternating) and take the
-// same lazy-rescale decision; warp half h rescales O columns [32 h, 32 h +
-// 32) and writes its P into P columns [32 h, 32 h + 32) (keys 64 h .. 64 h +
-// 63 as fp16 pairs), so the PV MMA reads the whole 128-key row.  Each half
-// keeps its own row sum; at the end of an item the halves add them and half
-// h normalises and stores head dims [32 h, 32 h + 32).  Barriers are named by
-// shared-memory address (one register each) to leave the registers to the
-// 64 scores a thread holds.
-__device__ __forceinline__ void softmax_half_rows(const AttnTile* __restrict__ tiles, int n_items, int chunk,
-                                                  bf16* __restrict__ out, int* err, uint32_t tmem_base,
-                                                  uint32_t sb) {
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const int hh = (warp - 4) >> 2;  // key half
-  const int q = warp & 3;          // TMEM lane quarter
-  const int r = q * 32 + lane;     // row inside the query block
-  const float sl2 = 0.125f * 1.4426950408889634f;
-  const uint32_t t_lane = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
-  const uint32_t abort_a = sb + OFF_ABORT;
-  const uint32_t my_x = sb + OFF_XMAX + static_cast<uint32_t>(hh * 128 + r) * 4;        // + 1024 per buffer
-  const uint32_t other_x = sb + OFF_XMAX + static_cast<uint32_t>((1 - hh) * 128 + r) * 4;
-  const uint32_t xbar = sb + OFF_XBAR + static_cast<uint32_t>(q) * 16;                  // + 8 per buffer
-  const uint32_t lbar = sb + OFF_LBAR + static_cast<uint32_t>(q) * 8;
-  const int grid = gridDim.x;
-  bool ok = true;
-  int g = 0;
-  // exchanges made so far by this quarter's warp pair (both warps of a pair
-  // make the same ones: items where their rows are all padding make none)
-  uint32_t xuse = 0, luse = 0;
-  for (int idx = blockIdx.x; ok && idx < n_items; idx += grid) {
-    const AttnItem it = load_item(tiles, idx, chunk);
-    const int qi = it.t.q0 + r;
-    int vis_end = it.t.seq_len;
-    if (chunk > 0) vis_end = min(vis_end, (qi / chunk + 1) * chunk);
-    float m_ref = -INFINITY;
-    float l = 0.f;
-    // both warps of a quarter hold the same rows: the same liveness
-    const bool live = __any_sync(0xffffffffu, r < it.nq);
-    for (int j = 0; j < it.nkv; ++j, ++g) {
-      ok = __all_sync(0xffffffffu, mbar_wait_a(sb + OFF_S_FULL, g & 1, err, abort_a, DEV_TIMEOUT_SOFTMAX));
-      if (!ok) break;
-      tc_fence_after();
-      if (!live) {
-        __syncwarp();
-        if (lane == 0) mbar_arrive_a(sb + OFF_S_EMPTY);
-        if (g > 0) {
-          ok = __all_sync(0xffffffffu,
-                          mbar_wait_a(sb + OFF_O_DONE, (g - 1) & 1, err, abort_a, DEV_TIMEOUT_SOFTMAX));
-          if (!ok) break;
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive_a(sb + OFF_P_FULL);
-        continue;
-      }
-      float sv[64];
-      tmem_ld32(t_lane + S_COL + 64 * hh, *reinterpret_cast<float(*)[32]>(sv));
-      tmem_ld32(t_lane + S_COL + 64 * hh + 32, *reinterpret_cast<float(*)[32]>(sv + 32));
-      tmem_ld_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_a(sb + OFF_S_EMPTY);
-
-      const int nvalid = vis_end - (j * 128 + 64 * hh);  // visible keys of this half (a prefix)
-      if (nvalid < 64) {
-#pragma unroll
-        for (int c = 0; c < 64; ++c) sv[c] = c < nvalid ? sv[c] : -INFINITY;
-      }
-      const int nv_warp = __reduce_max_sync(0xffffffffu, max(nvalid, 0));
-      float mx[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) mx[k] = fmaxf(sv[k], sv[k + 8]);
-#pragma unroll
-      for (int c = 16; c < 64; c += 16) {
-#pragma unroll
-        for (int k = 0; k < 8; ++k) mx[k] = max3(mx[k], sv[c + k], sv[c + 8 + k]);
-      }
-      const float hmax = max3(max3(mx[0], mx[1], mx[2]), max3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7])) * sl2;
-      // exchange the half maxima of the row; consecutive exchanges alternate
-      // buffers, so the partner's next write to this one comes after it
-      // passed the next exchange, which needs this thread's arrival (made
-      // after its read below)
-      const uint32_t xb = (xuse & 1u) * 1024u;
-      st_shared_f32(my_x + xb, hmax);
-      ok = pair_sync(xbar + (xuse & 1u) * 8u, (xuse >> 1) & 1u, err, abort_a);
-      ++xuse;
-      if (!ok) break;
-      const float m_cand = fmaxf(hmax, ld_shared_f32(other_x + xb));
-      const bool need = m_cand > m_ref + RESCALE_THRESHOLD;
-      // PV_{g-1} has read P_{g-1} and finished its update of O before this
-      // tile rescales O or replaces P (it was issued at the end of the last
-      // tile, so the wait is normally already satisfied)
-      if (g > 0) {
-        ok = __all_sync(0xffffffffu, mbar_wait_a(sb + OFF_O_DONE, (g - 1) & 1, err, abort_a, DEV_TIMEOUT_SOFTMAX));
-        if (!ok) break;
-        tc_fence_after();
-      }
-      if (__any_sync(0xffffffffu, need)) {
-        const float new_ref = need ? m_cand : m_ref;
-        const float alpha = need ? ex2(m_ref - new_ref) : 1.0f;
-        if (j > 0) {
-          float t[32];
-          tmem_ld32(t_lane + O_COL + 32 * hh, t);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) t[i] *= alpha;
-          tmem_st32(t_lane + O_COL + 32 * hh, t);
-        }
-        l *= alpha;
-        m_ref = new_ref;
-      }
-      const float m_use = (m_ref == -INFINITY) ? 0.f : m_ref;
-      float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
-#pragma unroll
-      for (int h = 0; h < 4; ++h) {
-        uint32_t pk[8];
-        if (16 * h < nv_warp) {
-          exp_chunk16(sv + 16 * h, sl2, m_use, acc0, acc1, pk);
-        } else {
-#pragma unroll
-          for (int i = 0; i < 8; ++i) pk[i] = 0u;
-        }
-        tmem_st8u(t_lane + P_COL + 32 * hh + 8 * h, pk);
-      }
-      l += (acc0.x + acc0.y) + (acc1.x + acc1.y);
-      tmem_st_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_a(sb + OFF_P_FULL);
-    }
-    if (!ok) break;
-    ok = __all_sync(0xffffffffu, mbar_wait_a(sb + OFF_O_DONE, (g - 1) & 1, err, abort_a, DEV_TIMEOUT_SOFTMAX));
-    if (!ok) break;
-    tc_fence_after();
-    if (!live) {
-      __syncwarp();
-      if (lane == 0) mbar_arrive_a(sb + OFF_O_FREE);
-      continue;
-    }
-    // the row sum of the whole row
-    st_shared_f32(sb + OFF_XSUM + static_cast<uint32_t>(hh * 128 + r) * 4, l);
-    ok = pair_sync(lbar, luse & 1u, err, abort_a);
-    ++luse;
-    if (!ok) break;
-    const float inv = 1.0f / (l + ld_shared_f32(sb + OFF_XSUM + static_cast<uint32_t>((1 - hh) * 128 + r) * 4));
-    float o[32];
-    tmem_ld32(t_lane + O_COL + 32 * hh, o);
-    tmem_ld_wait();
-    tc_fence_before();
-    __syncwarp();
-    if (lane == 0) mbar_arrive_a(sb + OFF_O_FREE);
-    if (r < it.nq) {
-      bf16* dst = out + static_cast<size_t>(it.t.seq_start + qi) * DIM + it.head * HDIM + 32 * hh;
-#pragma unroll
-      for (int c = 0; c < 2; ++c)
-        st_global_v8(dst + 16 * c, pack_bf16x2(o[16 * c + 0] * inv, o[16 * c + 1] * inv),
-                     pack_bf16x2(o[16 * c + 2] * inv, o[16 * c + 3] * inv),
-                     pack_bf16x2(o[16 * c + 4] * inv, o[16 * c + 5] * inv),
-                     pack_bf16x2(o[16 * c + 6] * inv, o[16 * c + 7] * inv),
-                     pack_bf16x2(o[16 * c + 8] * inv, o[16 * c + 9] * inv),
-                     pack_bf16x2(o[16 * c + 10] * inv, o[16 * c + 11] * inv),
-                     pack_bf16x2(o[16 * c + 12] * inv, o[16 * c + 13] * inv),
-                     pack_bf16x2(o[16 * c + 14] * inv, o[16 * c + 15] * inv));
-    }
-  }
-}
-
-template <int NWG>
-__global__ void __launch_bounds__(AttShape<NWG>::THREADS, 2)
+__global__ void __launch_bounds__(ATT_THREADS, 2)
     k_attention(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                 const __grid_constant__ CUtensorMap tmV, const AttnTile* __restrict__ tiles, int n_items, int chunk,
                 bf16* __restrict__ out, int* err) {
@@ -464,9 +213,6 @@ __global__ void __launch_bounds__(AttShape<NWG>::THREADS, 2)
   uint64_t* o_free = o_done + 1;  // the softmax has read the finished O of an item
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_free + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  // NWG = 2: the half-row exchange barriers (4 quarters x (2 buffers + 1))
-  uint64_t* xbar = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(bars) + OFF_XBAR);
-  constexpr int SMX_WARPS = 4 * NWG;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -484,12 +230,10 @@ __global__ void __launch_bounds__(AttShape<NWG>::THREADS, 2)
       mbar_init(&v_empty[s], 1);
     }
     mbar_init(s_full, 1);
-    mbar_init(s_empty, SMX_WARPS);
-    mbar_init(p_full, SMX_WARPS);
+    mbar_init(s_empty, 4);
+    mbar_init(p_full, 4);
     mbar_init(o_done, 1);
-    mbar_init(o_free, SMX_WARPS);
-    if (NWG == 2)
-      for (int i = 0; i < 12; ++i) mbar_init(&xbar[i], 2);  // the two warps of a lane quarter
+    mbar_init(o_free, 4);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -505,7 +249,7 @@ __global__ void __launch_bounds__(AttShape<NWG>::THREADS, 2)
   pdl_wait();
 
   if (warp < 4) {
-    regs_dec<AttShape<NWG>::PRODUCER>();
+    regs_dec<REGS_PRODUCER>();
     if (warp == 0) {
       if (lane == 0) {
         // Q of every item, then its K tiles (global step g: ring slot g % 2)
@@ -593,11 +337,8 @@ __global__ void __launch_bounds__(AttShape<NWG>::THREADS, 2)
         if (ok && g > 0) issue_pv_step(g - 1, prev_j, prev_n);
       }
     }
-  } else if constexpr (NWG == 2) {
-    regs_inc<AttShape<NWG>::SOFTMAX>();
-    softmax_half_rows(tiles, n_items, chunk, out, err, tmem_base, smem_u32(bars));
   } else {
-    regs_inc<AttShape<NWG>::SOFTMAX>();
+    regs_inc<REGS_SOFTMAX>();
     const int q = warp & 3;       // TMEM lane quarter
     const int r = q * 32 + lane;  // row inside the query block
     const float sl2 = 0.125f * 1.4426950408889634f;  // 1/sqrt(64) * log2(e)
@@ -781,44 +522,22 @@ __global__ void __launch_bounds__(AttShape<NWG>::THREADS, 2)
 
 }  // namespace
 
-namespace {
-
-// 1: the one-warpgroup softmax (a thread per query row); 2 (default): two
-// softmax warpgroups (a thread per half row).  LX_FLOW_ATT=1 selects the
-// first, for A/B measurements.
-int att_layout() {
-  static int v = 0;
-  if (!v) {
-    const char* e = getenv("LX_FLOW_ATT");
-    v = (e && e[0] == '1') ? 1 : 2;
-  }
-  return v;
-}
-
-template <int NWG>
-bool att_ready_for(int dev) {
+bool attention_ready() {
   static int checked[64] = {0};  // 0 unchecked, 1 ok, -1 unusable
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
   int& state = checked[dev & 63];
   if (state == 0) {
     // setmaxnreg.inc waits for registers the block was launched with: refuse
     // to launch unless the launch register count covers the split
     cudaFuncAttributes fa;
-    state = (cudaFuncGetAttributes(&fa, k_attention<NWG>) == cudaSuccess &&
-             fa.numRegs >= AttShape<NWG>::LAUNCH_REGS &&
-             cudaFuncSetAttribute(k_attention<NWG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  att_smem_bytes<NWG>()) == cudaSuccess)
+    state = (cudaFuncGetAttributes(&fa, k_attention) == cudaSuccess && fa.numRegs >= ATT_LAUNCH_REGS &&
+             cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, ATT_SMEM) ==
+                 cudaSuccess)
                 ? 1
                 : -1;
   }
   return state > 0;
-}
-
-}  // namespace
-
-bool attention_ready() {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return false;
-  return att_layout() == 2 ? att_ready_for<2>(dev) : att_ready_for<1>(dev);
 }
 
 bool attention(const CUtensorMap& Q, const CUtensorMap& K, const CUtensorMap& V, const AttnTile* tiles,
@@ -828,12 +547,7 @@ bool attention(const CUtensorMap& Q, const CUtensorMap& K, const CUtensorMap& V,
   // persistent: two CTAs per SM walk the (block, head) items
   const int n_items = n_tiles * HEADS;
   const int grid = n_items < 2 * num_sms() ? n_items : 2 * num_sms();
-  if (att_layout() == 2)
-    launch_pdl(k_attention<2>, dim3(grid), dim3(AttShape<2>::THREADS), att_smem_bytes<2>(), s, Q, K, V, tiles,
-               n_items, chunk, out, err);
-  else
-    launch_pdl(k_attention<1>, dim3(grid), dim3(AttShape<1>::THREADS), att_smem_bytes<1>(), s, Q, K, V, tiles,
-               n_items, chunk, out, err);
+  launch_pdl(k_attention, dim3(grid), dim3(ATT_THREADS), ATT_SMEM, s, Q, K, V, tiles, n_items, chunk, out, err);
   return true;
 }
 

@@ -104,49 +104,6 @@ __device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, in
   }
 }
 
-// The same waits on 32-bit shared-memory addresses (barrier and abort flag),
-// for code that keeps many barriers live: a shared address takes one register
-// where a generic pointer takes two.
-__device__ __forceinline__ void mbar_arrive_a(uint32_t bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait_a(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}\n"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity), "r"(hint_ns)
-      : "memory");
-  return ok != 0;
-}
-
-__device__ __forceinline__ int ld_shared_volatile(uint32_t a) {
-  int v;
-  asm volatile("ld.volatile.shared.u32 %0, [%1];" : "=r"(v) : "r"(a) : "memory");
-  return v;
-}
-
-__device__ __forceinline__ void st_shared_volatile(uint32_t a, int v) {
-  asm volatile("st.volatile.shared.u32 [%0], %1;" ::"r"(a), "r"(v) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_wait_a(uint32_t bar, uint32_t parity, int* err, uint32_t abort_flag, int code) {
-  if (mbar_try_wait_a(bar, parity, 0u)) return true;
-  const uint64_t t0 = global_timer_ns();
-  for (;;) {
-    if (mbar_try_wait_a(bar, parity, LX_WAIT_SUSPEND_NS)) return true;
-    if (ld_shared_volatile(abort_flag)) return false;
-    if (global_timer_ns() - t0 > LX_WAIT_TIMEOUT_NS) {
-      if (err) atomicCAS(err, 0, code);
-      st_shared_volatile(abort_flag, 1);
-      return false;
-    }
-  }
-}
-
 // The wait every kernel of the library uses: limit LX_WAIT_TIMEOUT_NS.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, volatile int* abort_flag,
                                           int code) {
