@@ -687,12 +687,19 @@ def main():
     ap.add_argument("--no-hift", action="store_true")
     ap.add_argument("--only-hift", action="store_true",
                     help="time only the HiFT vocoder (one 20 s utterance) and print its JSON object")
+    ap.add_argument("--only-cfg1", action="store_true",
+                    help="time only the config-1 fused-op microbench and print its JSON object")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     if args.only_hift:
         import torch
         print(json.dumps(bench_hift(torch.device("cuda", 0), with_cpu=not args.no_cpu)))
+        return
+    if args.only_cfg1:
+        import torch
+        dev = torch.device("cuda", 0)
+        print(json.dumps(bench_cfg1(dev, torch.cuda.Stream(device=dev))))
         return
     if args.impl == "reference":
         run_reference(args)

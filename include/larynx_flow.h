@@ -192,7 +192,9 @@ uint64_t lx_flow_launch_count(const lx_flow* h);
  * outputs are fp32.  op: 0 AdaLN-Zero modulated LayerNorm
  * (y = LN(x)(1+scale)+shift, src/flow/ops.cpp:94-104), 1 gate-residual
  * (x += gate * y, src/flow/dit.cpp:71,77), 2 partial rotary (channels 0..63,
- * pos[row], src/flow/ops.cpp:85-92), 3 GELU-tanh (src/flow/ops.cpp:73-83). */
+ * pos[row], src/flow/ops.cpp:85-92), 3 GELU-tanh (src/flow/ops.cpp:73-83).
+ * Launched with programmatic dependent launch: an op may begin while the
+ * stream's previous kernel finishes and waits for it before reading memory. */
 int lx_flow_op(int op, int in_bf16, int rows, const void* x, void* y, const float* shift, const float* scale,
                const float* gate, const int32_t* pos, void* stream);
 

@@ -46,8 +46,8 @@ template <typename Tin, typename Tout>
 __global__ void __launch_bounds__(512) k_adaln(const Tin* __restrict__ x, Tout* __restrict__ y,
                                                 const float* __restrict__ shift, const float* __restrict__ scale,
                                                 int R) {
-  pdl_launch_dependents();
   pdl_wait();
+  pdl_launch_dependents();  // after the wait: at most one dependent launch ahead
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= R) return;
@@ -308,8 +308,8 @@ __global__ void k_front_mu_cond(const float* __restrict__ pre, int n_tok, const 
 template <typename Tin>
 __global__ void k_gate_res(float* __restrict__ x, const Tin* __restrict__ y, const float* __restrict__ gate,
                            size_t n4) {
-  pdl_launch_dependents();
   pdl_wait();
+  pdl_launch_dependents();  // after the wait: at most one dependent launch ahead
   const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= n4) return;
   const int c = static_cast<int>((i * 4) % DIM);
@@ -329,8 +329,8 @@ template <typename Tin>
 __global__ void __launch_bounds__(512) k_rotary(const Tin* __restrict__ x, float* __restrict__ y,
                                                  const int* __restrict__ pos, const float2* __restrict__ rope,
                                                  int R) {
-  pdl_launch_dependents();
   pdl_wait();
+  pdl_launch_dependents();  // after the wait: at most one dependent launch ahead
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= R) return;
@@ -353,8 +353,8 @@ __global__ void __launch_bounds__(512) k_rotary(const Tin* __restrict__ x, float
 
 template <typename Tin>
 __global__ void k_gelu(const Tin* __restrict__ x, float* __restrict__ y, size_t n4) {
-  pdl_launch_dependents();
   pdl_wait();
+  pdl_launch_dependents();  // after the wait: at most one dependent launch ahead
   const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= n4) return;
   float4 v = load4(x + i * 4);

@@ -1222,6 +1222,14 @@ int lx_flow_op(int op, int in_bf16, int rows, const void* x, void* y, const floa
                const float* gate, const int32_t* pos, void* stream) {
   if (rows < 0 || !x || !y) return LX_ERR_ARG;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // Programmatic dependent launch (unless LX_FLOW_PDL=0): the op may start
+  // while the previous kernel of the stream drains; its blocks wait inside
+  // before touching memory, so any predecessor is safe.  In a chain of short
+  // ops one launch's ramp then overlaps the last one's tail.
+  struct PdlOn {
+    PdlOn() { pdl_set_auto(true); }
+    ~PdlOn() { pdl_set_auto(false); }
+  } pdl_on;
   switch (op) {
     case 0:
       if (!shift || !scale) return LX_ERR_ARG;
