@@ -571,12 +571,16 @@ def run_ours(args):
     g_n = sum(prof[k][1] for k in gem)
     g_fl = sum(algorithmic_per_launch(k, lengths)[0] * prof[k][1] for k in gem)
     achieved = g_fl / (g_ms * 1e-3) / 1e12
+    # ncu traffic of a smaller capture, scaled to this rank's packed rows
+    # (two CFG sequences per utterance, each padded to 8 rows)
+    rows = int(2 * np.sum((np.asarray(lengths) + 7) // 8 * 8))
+    rs = rows / float(traffic.get("rows_bench", rows) or rows)
     tr = [traffic.get(k, {}).get("bytes_per_launch_scaled") for k in gem]
-    traffic_pl = (sum(t * prof[k][1] for t, k in zip(tr, gem)) / g_n) if all(tr) else None
+    traffic_pl = (sum(t * rs * prof[k][1] for t, k in zip(tr, gem)) / g_n) if all(tr) else None
     alg_bytes = None
     if traffic.get("algorithmic_bytes_per_launch"):
         ab = traffic["algorithmic_bytes_per_launch"]
-        alg_bytes = sum(ab[k] * prof[k][1] for k in gem) / g_n if all(k in ab for k in gem) else None
+        alg_bytes = sum(ab[k] * rs * prof[k][1] for k in gem) / g_n if all(k in ab for k in gem) else None
     roofline = {"kernel": "k_gemm2 (tcgen05 CTA-pair GEMM: QKV, out, FF1, FF2 projections)", "bound": "tensor",
                 "achieved": achieved, "peak": peaks["tensor"], "unit": "TFLOP/s", "frac": achieved / peaks["tensor"],
                 "traffic": traffic_pl, "traffic_unit": "bytes per launch (ncu dram read+write, scaled)",
