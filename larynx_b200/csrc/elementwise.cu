@@ -2,7 +2,6 @@
 // LayerNorm, the CFG Euler update, layout gathers/scatters, the load-time
 // time-embedding / modulation GEMVs, the once-per-utterance frontend, and the
 // standalone fused ops timed by the microbench.
-#include "adaln_row.cuh"
 #include "common.cuh"
 #include "kernels.h"
 
@@ -40,8 +39,9 @@ __device__ __forceinline__ void store4(bf16* p, float4 v) {
   *reinterpret_cast<uint2*>(p) = u;
 }
 
-// One warp per 1024-wide row (adaln_row.cuh; the same routine runs fused
-// into the residual GEMM's epilogue).
+// One warp per 1024-wide row; lane owns columns 4*lane + 128*i, i < 8.
+// Two-pass statistics in registers (mean, then centred variance), biased
+// variance, eps 1e-6, then (x - mean) * rstd * (1 + scale) + shift.
 template <typename Tin, typename Tout>
 __global__ void __launch_bounds__(512) k_adaln(const Tin* __restrict__ x, Tout* __restrict__ y,
                                                 const float* __restrict__ shift, const float* __restrict__ scale,
@@ -49,9 +49,38 @@ __global__ void __launch_bounds__(512) k_adaln(const Tin* __restrict__ x, Tout* 
   pdl_wait();
   pdl_launch_dependents();  // after the wait: at most one dependent launch ahead
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
   if (row >= R) return;
-  const int rows[1] = {row};
-  adaln_rows_warp<1>(x, y, rows, shift, scale, threadIdx.x & 31);
+  const Tin* xr = x + static_cast<size_t>(row) * DIM;
+  float4 v[8];
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    v[i] = load4(xr + 4 * lane + 128 * i);
+    s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+  }
+  const float mean = warp_sum(s) * (1.0f / DIM);
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float a = v[i].x - mean, b = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
+    q += (a * a + b * b) + (c * c + d * d);
+  }
+  const float var = warp_sum(q) * (1.0f / DIM);
+  const float rstd = 1.0f / sqrtf(var + 1e-6f);
+  Tout* yr = y + static_cast<size_t>(row) * DIM;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int c = 4 * lane + 128 * i;
+    const float4 sc = __ldg(reinterpret_cast<const float4*>(scale + c));
+    const float4 sh = __ldg(reinterpret_cast<const float4*>(shift + c));
+    float4 o;
+    o.x = (v[i].x - mean) * rstd * (1.0f + sc.x) + sh.x;
+    o.y = (v[i].y - mean) * rstd * (1.0f + sc.y) + sh.y;
+    o.z = (v[i].z - mean) * rstd * (1.0f + sc.z) + sh.z;
+    o.w = (v[i].w - mean) * rstd * (1.0f + sc.w) + sh.w;
+    store4(yr + c, o);
+  }
 }
 
 // CFG Euler step (src/flow/flow.cpp:257-259 order):

@@ -471,8 +471,7 @@ int ensure_workspace(lx_flow* h, const Plan& p, size_t in_floats, int n_utt) {
                      (void**)&w.dphi,    (void**)&w.xs,        (void**)&w.pos,      (void**)&w.p2s,
                      (void**)&w.s2p,     (void**)&w.frame_utt, (void**)&w.seq_rows, (void**)&w.frame_rows,
                      (void**)&w.frame_src, (void**)&w.tiles,   (void**)&w.in_mu,    (void**)&w.in_cond,
-                     (void**)&w.in_noise, (void**)&w.out_mel,  (void**)&w.in_spks,  (void**)&w.cap,
-                     (void**)&w.ln_cnt};
+                     (void**)&w.in_noise, (void**)&w.out_mel,  (void**)&w.in_spks,  (void**)&w.cap};
     for (void** pp : ptrs) wsfree(*pp);
     w.capCap = 0;
     // grow with headroom so that nearby shapes reuse the allocation
@@ -498,10 +497,8 @@ int ensure_workspace(lx_flow* h, const Plan& p, size_t in_floats, int n_utt) {
         (rc = dev_alloc(h, &w.tiles, static_cast<size_t>(w.capTiles), false)) ||
         (rc = dev_alloc(h, &w.in_mu, w.capIn, false)) || (rc = dev_alloc(h, &w.in_cond, w.capIn, false)) ||
         (rc = dev_alloc(h, &w.in_noise, w.capIn, false)) || (rc = dev_alloc(h, &w.out_mel, w.capIn, false)) ||
-        (rc = dev_alloc(h, &w.in_spks, w.capUtt * MEL, false)) ||
-        (rc = dev_alloc(h, &w.ln_cnt, R / 128 + 4, false)))
+        (rc = dev_alloc(h, &w.in_spks, w.capUtt * MEL, false)))
       return rc;
-    CK(cudaMemset(w.ln_cnt, 0, (R / 128 + 4) * sizeof(int)));
     // every buffer starts finite: rows that no kernel writes (alignment gaps,
     // rows past the last sequence, staging gap rows) are read as operands
     CK(cudaMemset(w.x, 0, R * DIM * 4));
@@ -592,9 +589,6 @@ void enqueue_dit(lx_flow* h, const Plan& p, const float* mod, const float* mod_f
   const int bn1024 = pick_bn(R, DIM), bnq = pick_bn(R, QKV_N), bnf = pick_bn(R, FF);
   const int i1024 = bn1024 == 256, iq = bnq == 256, iff = bnf == 256;
   const bool pair_q = use_pair_gemm(R, QKV_N), pair_f = use_pair_gemm(R, FF), pair_d = use_pair_gemm(R, DIM);
-  // the residual GEMMs produce the next AdaLN themselves (post-pass) when
-  // they run on CTA pairs
-  const bool fuse_ln = pair_d && fuse_ln_enabled();
   int* err = h->d_err;
   timed(h, K_INPROJ, s, [&] { gemm_in_proj(bn1024, w.tm_xb, W.tm_winx[i1024], R, w.cst, w.x, w.stage1, w.p2s, err, s); });
   timed(h, K_CONV, s, [&] { conv_pos(w.tm_stage1, W.tm_wconv[0], p.Rs, W.bconv[0], 0, w.stage2, w.x, w.s2p, err, s); });
@@ -607,14 +601,7 @@ void enqueue_dit(lx_flow* h, const Plan& p, const float* mod, const float* mod_f
   for (int l = 0; l < DEPTH; ++l) {
     // modulation chunks: shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp
     const float* m = mod + static_cast<size_t>(l) * MOD_N;
-    // the next AdaLN after this block's FF2: block l + 1's attention norm, or
-    // the final norm (chunk order scale, shift: flow_reference.py:192)
-    const float* next_shift = l + 1 < DEPTH ? m + MOD_N : mod_final + DIM;
-    const float* next_scale = l + 1 < DEPTH ? m + MOD_N + DIM : mod_final;
-    if (l == 0 || !fuse_ln) {
-      timed(h, K_ADALN, s, [&] { adaln_rows(w.x, w.xn, m + 0 * DIM, m + 1 * DIM, R, s); });
-      ++h->launches;
-    }
+    timed(h, K_ADALN, s, [&] { adaln_rows(w.x, w.xn, m + 0 * DIM, m + 1 * DIM, R, s); });
     timed(h, K_QKV, s, [&] {
       if (pair_q)
         gemm_pair_qkv(w.tm_xn, W.tm_wqkv[0], R, l * QKV_N, W.bqkv + static_cast<size_t>(l) * QKV_N, w.q, w.k, w.v,
@@ -626,20 +613,14 @@ void enqueue_dit(lx_flow* h, const Plan& p, const float* mod, const float* mod_f
     timed(h, K_ATTN, s,
           [&] { attention(w.tm_q, w.tm_k, w.tm_v, w.tiles, static_cast<int>(p.tiles.size()), chunk, w.ao, err, s); });
     timed(h, K_OUT, s, [&] {
-      if (fuse_ln)
-        gemm_pair_gate_res_ln(w.tm_ao, W.tm_wo[0], w.tm_x, R, DIM, l * DIM, W.bo + static_cast<size_t>(l) * DIM,
-                              m + 2 * DIM, w.x, w.xn, m + 3 * DIM, m + 4 * DIM, w.ln_cnt, err, s);
-      else if (pair_d)
+      if (pair_d)
         gemm_pair_gate_res(w.tm_ao, W.tm_wo[0], w.tm_x, R, DIM, l * DIM, W.bo + static_cast<size_t>(l) * DIM,
                            m + 2 * DIM, w.x, err, s);
       else
         gemm_gate_res_tma(w.tm_ao, W.tm_wo[0], w.tm_x, R, DIM, l * DIM, W.bo + static_cast<size_t>(l) * DIM,
                           m + 2 * DIM, w.x, err, s);
     });
-    if (!fuse_ln) {
-      timed(h, K_ADALN, s, [&] { adaln_rows(w.x, w.xn, m + 3 * DIM, m + 4 * DIM, R, s); });
-      ++h->launches;
-    }
+    timed(h, K_ADALN, s, [&] { adaln_rows(w.x, w.xn, m + 3 * DIM, m + 4 * DIM, R, s); });
     timed(h, K_FF1, s, [&] {
       if (pair_f)
         gemm_pair_gelu(w.tm_xn, W.tm_w1[0], R, l * FF, W.b1 + static_cast<size_t>(l) * FF, w.h, err, s);
@@ -647,17 +628,14 @@ void enqueue_dit(lx_flow* h, const Plan& p, const float* mod, const float* mod_f
         gemm_gelu(bnf, w.tm_xn, W.tm_w1[iff], R, l * FF, W.b1 + static_cast<size_t>(l) * FF, w.h, err, s);
     });
     timed(h, K_FF2, s, [&] {
-      if (fuse_ln)
-        gemm_pair_gate_res_ln(w.tm_h, W.tm_w2[0], w.tm_x, R, FF, l * DIM, W.b2 + static_cast<size_t>(l) * DIM,
-                              m + 5 * DIM, w.x, w.xn, next_shift, next_scale, w.ln_cnt, err, s);
-      else if (pair_d)
+      if (pair_d)
         gemm_pair_gate_res(w.tm_h, W.tm_w2[0], w.tm_x, R, FF, l * DIM, W.b2 + static_cast<size_t>(l) * DIM,
                            m + 5 * DIM, w.x, err, s);
       else
         gemm_gate_res_tma(w.tm_h, W.tm_w2[0], w.tm_x, R, FF, l * DIM, W.b2 + static_cast<size_t>(l) * DIM,
                           m + 5 * DIM, w.x, err, s);
     });
-    h->launches += 5;
+    h->launches += 7;
     if (cap && cap->block && cap->block_index == l) {
       gather_rows(cap->block, w.x, w.seq_rows, p.F, DIM, s);
       ++h->launches;
@@ -667,14 +645,10 @@ void enqueue_dit(lx_flow* h, const Plan& p, const float* mod, const float* mod_f
       ++h->launches;
     }
   }
-  // AdaLayerNormZero_Final: chunk order scale, shift (flow_reference.py:192);
-  // with the fused post-pass the last FF2 has written it already
-  if (!fuse_ln) {
-    timed(h, K_ADALN, s, [&] { adaln_rows(w.x, w.xn, mod_final + DIM, mod_final, R, s); });
-    ++h->launches;
-  }
+  // AdaLayerNormZero_Final: chunk order scale, shift (flow_reference.py:192)
+  timed(h, K_ADALN, s, [&] { adaln_rows(w.x, w.xn, mod_final + DIM, mod_final, R, s); });
   timed(h, K_PROJOUT, s, [&] { gemm_f32(128, w.tm_xn, W.tm_wout, R, MEL, DIM, W.bout, w.dphi, MEL, err, s); });
-  ++h->launches;
+  h->launches += 2;
   if (cap && cap->norm_out) {
     gather_rows_bf16(cap->norm_out, w.xn, w.seq_rows, p.F, DIM, s);
     ++h->launches;

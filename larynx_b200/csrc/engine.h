@@ -83,7 +83,6 @@ struct Workspace {
   AttnTile* tiles = nullptr;
   float *in_mu = nullptr, *in_cond = nullptr, *in_noise = nullptr, *out_mel = nullptr, *in_spks = nullptr;
   float* cap = nullptr;  // capture scratch [R][1024]
-  int* ln_cnt = nullptr;  // per-128-row-block counters of the fused AdaLN post-pass (kept zero)
   size_t capCap = 0;
   CUtensorMap tm_xn, tm_ao, tm_h, tm_xb, tm_acond, tm_stage1, tm_stage2, tm_q, tm_k, tm_v;
   CUtensorMap tm_x;  // fp32 residual stream, box 128 x 32

@@ -212,20 +212,6 @@ struct EpiGateResSmem {
   }
 };
 
-// EpiGateResSmem whose k_gemm2 post-pass also writes the next AdaLN-modulated
-// LayerNorm xn = LN(x) (1 + scale) + shift of every 128-row block it completes;
-// cnt: one zero-initialised counter per 128-row block (left zero again).
-struct EpiGateResLN : EpiGateResSmem {
-  bf16* xn;
-  const float* shift;
-  const float* scale;
-  int* cnt;
-};
-template <>
-struct EpiPostLN<EpiGateResLN> {
-  static constexpr bool value = true;
-};
-
 struct EpiGelu {
   const float* bias;
   bf16* h;
@@ -394,33 +380,10 @@ void gemm_pair_gate_res(const CUtensorMap& A, const CUtensorMap& B, const CUtens
   launch_pair<5, true, 2>(A, B, M, DIM, K, b_off, e, err, s, &X);
 }
 
-void gemm_pair_gate_res_ln(const CUtensorMap& A, const CUtensorMap& B, const CUtensorMap& X, int M, int K, int b_off,
-                           const float* bias, const float* gate, float* x, bf16* xn, const float* shift,
-                           const float* scale, int* cnt, int* err, cudaStream_t s) {
-  EpiGateResLN e;
-  e.bias = bias;
-  e.gate = gate;
-  e.x = x;
-  e.xn = xn;
-  e.shift = shift;
-  e.scale = scale;
-  e.cnt = cnt;
-  launch_pair<5, true, 2>(A, B, M, DIM, K, b_off, e, err, s, &X);
-}
-
 void gemm_pair_f32(const CUtensorMap& A, const CUtensorMap& B, int M, int N, int K, const float* bias, float* out,
                    int ldo, int* err, cudaStream_t s) {
   EpiF32 e{bias, out, ldo};
   launch_pair<6, false, 0>(A, B, M, N, K, 0, e, err, s);
-}
-
-bool fuse_ln_enabled() {
-  static int env = -1;
-  if (env < 0) {
-    const char* e = getenv("LX_FLOW_FUSE_LN");
-    env = (e && e[0] == '0') ? 0 : 1;
-  }
-  return env != 0;
 }
 
 bool use_pair_gemm(int M, int N) {

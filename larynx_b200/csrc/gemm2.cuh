@@ -29,7 +29,6 @@
 // Every TMA copy in this file lands in the issuing CTA's own shared memory.
 #pragma once
 
-#include "adaln_row.cuh"
 #include "common.cuh"
 #include "gemm.cuh"
 
@@ -128,20 +127,6 @@ __device__ __forceinline__ void umma_pair_commit(uint32_t bar_cluster) {
   asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_cluster)
                : "memory");
 }
-
-// Residual epilogues that also produce the next AdaLN-modulated LayerNorm
-// (see the post-pass in k_gemm2) specialise this to true.
-template <class Epi>
-struct EpiPostLN {
-  static constexpr bool value = false;
-};
-
-// Rows of the post-pass each epilogue warp normalises at once (their loads in flight together).
-#ifndef POST_ROWS_OVERRIDE
-constexpr int POST_ROWS = 1;
-#else
-constexpr int POST_ROWS = POST_ROWS_OVERRIDE;
-#endif
 
 // 12 warps: 0 TMA, 1 MMA/TMEM, 2 residual loader (RES), 3 idle, 4..11 epilogue.
 constexpr int GEMM2_THREADS = 384;
@@ -245,9 +230,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM2_THREADS, 1)
   uint64_t* x_empty = x_full + XS_;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(x_empty + XS_);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  // post-pass (EpiPostLN): the epilogue warps' per-tile hand-shake
-  uint64_t* post_bar = reinterpret_cast<uint64_t*>(tmem_slot + 2);
-  volatile int* post_last = reinterpret_cast<volatile int*>(post_bar + 1);  // [2 tiles][8 warps]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -266,7 +248,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM2_THREADS, 1)
       mbar_init(&x_full[s], 1);
       mbar_init(&x_empty[s], 8);
     }
-    if (EpiPostLN<Epi>::value) mbar_init(post_bar, 8);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -397,7 +378,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM2_THREADS, 1)
     uint32_t acc_phase = 0;
     int slot = 0;
     uint32_t xph = 0;
-    uint32_t ntile = 0;
     for (int tile = pair; tile < n_tiles; tile += n_pairs) {
       const int m0 = (tile / tiles_n) * G2_BM + static_cast<int>(rank) * G2_HALF;
       const int n0 = (tile % tiles_n) * G2_BN + cb;
@@ -435,48 +415,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM2_THREADS, 1)
       }
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
-      if constexpr (EpiPostLN<Epi>::value) {
-        // Post-pass: the residual rows [m0, m0 + 128) of this CTA are final
-        // once all tiles_n column tiles of them are stored (by whichever
-        // CTAs ran them).  Every epilogue warp fences its stores and counts
-        // them on the block's counter; the warp that brings it to 8 x tiles_n
-        // resets it for the next launch, and its CTA's 8 epilogue warps then
-        // apply the next AdaLN-modulated LayerNorm to those 128 rows (x fp32,
-        // just written and still in L2, -> xn bf16): the standalone AdaLN
-        // pass over the whole residual stream is not needed.
-        const int blk = m0 / G2_HALF;
-        __threadfence();
-        __syncwarp();
-        int last = 0;
-        if (lane == 0) {
-          last = atomicAdd(epi.cnt + blk, 1) == 8 * tiles_n - 1;
-          if (last) epi.cnt[blk] = 0;
-        }
-        volatile int* slots = post_last + (ntile & 1u) * 8;
-        if (lane == 0) slots[warp - G2_EPI_WARP0] = last;
-        __syncwarp();
-        if (lane == 0) mbar_arrive(post_bar);
-        ok = mbar_wait(post_bar, ntile & 1u, sh.err, abort_flag, DEV_TIMEOUT_EPILOGUE);
-        if (!__all_sync(0xffffffffu, ok)) break;
-        int any = 0;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) any |= slots[i];
-        ++ntile;
-        if (any) {
-          __threadfence();  // the other CTAs' stores of the block, counted before the last increment
-          const int e = warp - G2_EPI_WARP0;
-#pragma unroll 1
-          for (int r0 = 0; r0 < 16; r0 += POST_ROWS) {
-            int rows[POST_ROWS];
-#pragma unroll
-            for (int k = 0; k < POST_ROWS; ++k) {
-              const int rr = m0 + 16 * e + r0 + k;
-              rows[k] = rr < sh.M ? rr : -1;
-            }
-            adaln_rows_warp<POST_ROWS>(static_cast<const float*>(epi.x), epi.xn, rows, epi.shift, epi.scale, lane);
-          }
-        }
-      }
     }
   }
 

@@ -135,14 +135,6 @@ void gemm_pair_gelu(const CUtensorMap& A, const CUtensorMap& B, int M, int b_off
                     int* err, cudaStream_t s);
 void gemm_pair_gate_res(const CUtensorMap& A, const CUtensorMap& B, const CUtensorMap& X, int M, int K, int b_off,
                         const float* bias, const float* gate, float* x, int* err, cudaStream_t s);
-// gemm_pair_gate_res followed, per 128-row block, by the next AdaLN-modulated
-// LayerNorm of the finished residual rows: xn = LN(x) (1 + scale) + shift
-// (bf16).  cnt: ceil(M / 128) zero-initialised ints, left zero.
-void gemm_pair_gate_res_ln(const CUtensorMap& A, const CUtensorMap& B, const CUtensorMap& X, int M, int K, int b_off,
-                           const float* bias, const float* gate, float* x, bf16* xn, const float* shift,
-                           const float* scale, int* cnt, int* err, cudaStream_t s);
-// LX_FLOW_FUSE_LN=0 turns the fused AdaLN post-pass off (standalone AdaLN).
-bool fuse_ln_enabled();
 // causal grouped conv (k=31, 16 groups) over the staged rows [0, Ms); B box 64 x 64.
 // second == 0: out_stage[srow] = bf16(mish(conv + bias))  (rows with s2p >= 0)
 // second == 1: x[s2p[srow]] += mish(conv + bias)

@@ -151,37 +151,3 @@ def test_cfg4_ctx500_streams_vs_oracle(dec):
     chunk + 6 look-ahead), block-causal chunk mask 50, 10-step CFG decode
     (8896 packed rows: QKV and FF1 on the pair kernel)."""
     _decode_vs_fixture(dec, CFG4, "oracle_cfg4_ctx500.npz")
-
-
-_DECODE_CHILD = """
-import sys, numpy as np
-sys.path.insert(0, sys.argv[1])
-from larynx_b200 import FlowDecoder
-d = np.load(sys.argv[3])
-dec = FlowDecoder(0)
-assert dec.load(sys.argv[2]), dec.last_error
-L = [int(n) for n in d['lengths']]
-out = dec.decode(L, d['mu'], d['cond'], d['spks'], noise=d['noise'], n_steps=2)
-np.save(sys.argv[4], out)
-"""
-
-
-def test_fused_adaln_post_pass_is_bit_identical(dec, gguf_path, tmp_path):
-    """At config-3 scale the residual GEMMs (out, FF2) write the next AdaLN
-    themselves (a post-pass per finished 128-row block) instead of a separate
-    AdaLN kernel.  Both run the same row routine: a 2-step decode of the 8
-    config-3 utterances must be bit-identical with the post-pass on (this
-    process) and off (LX_FLOW_FUSE_LN=0, a child process)."""
-    lengths, mus, conds, spks, noises = _cfg3_subset()
-    got = dec.decode(lengths, mus, conds, spks, noise=noises, n_steps=2)
-    inp = str(tmp_path / "in.npz")
-    np.savez(inp, lengths=np.asarray(lengths, np.int32), mu=_flat(mus), cond=_flat(conds), spks=spks,
-             noise=_flat(noises))
-    ref_path = str(tmp_path / "ref.npy")
-    env = dict(os.environ, LX_FLOW_FUSE_LN="0")
-    r = subprocess.run([sys.executable, "-c", _DECODE_CHILD, REPO, gguf_path, inp, ref_path], env=env,
-                       capture_output=True, text=True, timeout=600)
-    assert r.returncode == 0, r.stderr[-2000:]
-    ref = np.load(ref_path)
-    assert np.isfinite(got).all()
-    np.testing.assert_array_equal(got, ref)
