@@ -9,6 +9,14 @@ namespace lx {
 
 namespace {
 
+// Bring [p, p + bytes) into L2 (16-byte aligned, bytes a multiple of 16).
+// Issued before pdl_wait by the standalone ops: L2 is coherent, so lines the
+// previous kernel is still writing are read correctly after the wait, and
+// inputs it does not write arrive early.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -42,14 +50,15 @@ __device__ __forceinline__ void store4(bf16* p, float4 v) {
 // One warp per 1024-wide row; lane owns columns 4*lane + 128*i, i < 8.
 // Two-pass statistics in registers (mean, then centred variance), biased
 // variance, eps 1e-6, then (x - mean) * rstd * (1 + scale) + shift.
-template <typename Tin, typename Tout>
+template <typename Tin, typename Tout, bool PF = false>
 __global__ void __launch_bounds__(512) k_adaln(const Tin* __restrict__ x, Tout* __restrict__ y,
                                                 const float* __restrict__ shift, const float* __restrict__ scale,
                                                 int R) {
-  pdl_wait();
-  pdl_launch_dependents();  // after the wait: at most one dependent launch ahead
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
+  if (PF && row < R && lane == 0) prefetch_l2_bulk(x + static_cast<size_t>(row) * DIM, DIM * sizeof(Tin));
+  pdl_wait();
+  pdl_launch_dependents();  // after the wait: at most one dependent launch ahead
   if (row >= R) return;
   const Tin* xr = x + static_cast<size_t>(row) * DIM;
   float4 v[8];
@@ -308,6 +317,11 @@ __global__ void k_front_mu_cond(const float* __restrict__ pre, int n_tok, const 
 template <typename Tin>
 __global__ void k_gate_res(float* __restrict__ x, const Tin* __restrict__ y, const float* __restrict__ gate,
                            size_t n4) {
+  const size_t b0 = static_cast<size_t>(blockIdx.x) * blockDim.x;
+  if (threadIdx.x == 0 && b0 + blockDim.x <= n4) {
+    prefetch_l2_bulk(x + b0 * 4, blockDim.x * 16);
+    prefetch_l2_bulk(y + b0 * 4, blockDim.x * 4 * sizeof(Tin));
+  }
   pdl_wait();
   pdl_launch_dependents();  // after the wait: at most one dependent launch ahead
   const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -329,10 +343,19 @@ template <typename Tin>
 __global__ void __launch_bounds__(512) k_rotary(const Tin* __restrict__ x, float* __restrict__ y,
                                                  const int* __restrict__ pos, const float2* __restrict__ rope,
                                                  int R) {
-  pdl_wait();
-  pdl_launch_dependents();  // after the wait: at most one dependent launch ahead
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
+  // The table row of this row's position into L2 before the wait.  pos may
+  // still be being written by the previous kernel: the value read here only
+  // picks (clamped) lines to prefetch, and pos is read again after the wait.
+  // (Prefetching the row of x as well made this op slower: measured.)
+  if (row < R && lane == 0) {
+    int p = pos[row];
+    p = p < 0 ? 0 : (p >= ROPE_MAX ? ROPE_MAX - 1 : p);
+    prefetch_l2_bulk(rope + static_cast<size_t>(p) * 32, 32 * sizeof(float2));
+  }
+  pdl_wait();
+  pdl_launch_dependents();  // after the wait: at most one dependent launch ahead
   if (row >= R) return;
   const Tin* xr = x + static_cast<size_t>(row) * DIM;
   float* yr = y + static_cast<size_t>(row) * DIM;
@@ -353,6 +376,8 @@ __global__ void __launch_bounds__(512) k_rotary(const Tin* __restrict__ x, float
 
 template <typename Tin>
 __global__ void k_gelu(const Tin* __restrict__ x, float* __restrict__ y, size_t n4) {
+  const size_t b0 = static_cast<size_t>(blockIdx.x) * blockDim.x;
+  if (threadIdx.x == 0 && b0 + blockDim.x <= n4) prefetch_l2_bulk(x + b0 * 4, blockDim.x * 4 * sizeof(Tin));
   pdl_wait();
   pdl_launch_dependents();  // after the wait: at most one dependent launch ahead
   const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -437,10 +462,10 @@ void frontend_mu_cond(const float* pre, int n_tok, const float* prompt_feat, int
 }
 
 void op_adaln_f32(const float* x, float* y, const float* shift, const float* scale, int R, cudaStream_t s) {
-  if (R > 0) launch_pdl(k_adaln<float, float>, dim3((R + rows_per_block(R) - 1) / rows_per_block(R)), dim3(32 * rows_per_block(R)), 0, s, x, y, shift, scale, R);
+  if (R > 0) launch_pdl(k_adaln<float, float, true>, dim3((R + rows_per_block(R, 0) - 1) / rows_per_block(R, 0)), dim3(32 * rows_per_block(R, 0)), 0, s, x, y, shift, scale, R);
 }
 void op_adaln_bf16(const bf16* x, float* y, const float* shift, const float* scale, int R, cudaStream_t s) {
-  if (R > 0) launch_pdl(k_adaln<bf16, float>, dim3((R + rows_per_block(R) - 1) / rows_per_block(R)), dim3(32 * rows_per_block(R)), 0, s, x, y, shift, scale, R);
+  if (R > 0) launch_pdl(k_adaln<bf16, float, true>, dim3((R + rows_per_block(R, 0) - 1) / rows_per_block(R, 0)), dim3(32 * rows_per_block(R, 0)), 0, s, x, y, shift, scale, R);
 }
 void op_gate_res_f32(float* x, const float* y, const float* gate, int R, cudaStream_t s) {
   const size_t n4 = static_cast<size_t>(R) * DIM / 4;
@@ -451,10 +476,10 @@ void op_gate_res_bf16(float* x, const bf16* y, const float* gate, int R, cudaStr
   if (n4) launch_pdl(k_gate_res<bf16>, dim3(blocks_for(n4, 256)), dim3(256), 0, s, x, y, gate, n4);
 }
 void op_rotary_f32(const float* x, float* y, const int* pos, const float2* rope, int R, cudaStream_t s) {
-  if (R > 0) launch_pdl(k_rotary<float>, dim3((R + rows_per_block(R) - 1) / rows_per_block(R)), dim3(32 * rows_per_block(R)), 0, s, x, y, pos, rope, R);
+  if (R > 0) launch_pdl(k_rotary<float>, dim3((R + rows_per_block(R, 0) - 1) / rows_per_block(R, 0)), dim3(32 * rows_per_block(R, 0)), 0, s, x, y, pos, rope, R);
 }
 void op_rotary_bf16(const bf16* x, float* y, const int* pos, const float2* rope, int R, cudaStream_t s) {
-  if (R > 0) launch_pdl(k_rotary<bf16>, dim3((R + rows_per_block(R) - 1) / rows_per_block(R)), dim3(32 * rows_per_block(R)), 0, s, x, y, pos, rope, R);
+  if (R > 0) launch_pdl(k_rotary<bf16>, dim3((R + rows_per_block(R, 0) - 1) / rows_per_block(R, 0)), dim3(32 * rows_per_block(R, 0)), 0, s, x, y, pos, rope, R);
 }
 void op_gelu_f32(const float* x, float* y, size_t n, cudaStream_t s) {
   if (n >= 4) launch_pdl(k_gelu<float>, dim3(blocks_for(n / 4, 256)), dim3(256), 0, s, x, y, n / 4);

@@ -13,7 +13,6 @@ namespace lx {
 
 constexpr int N_STEPS_DEFAULT = 10;
 constexpr float CFG_RATE = 0.7f;
-constexpr int ROPE_MAX = 16384;      // positions covered by the rotary table
 constexpr int SEQ_ALIGN = 8;         // packed sequences start on 8-row boundaries (as lx_flow_op_attention)
 constexpr int STAGE_GAP = 32;        // zero rows before each sequence in the conv staging layout (>= k-1 = 30)
 constexpr int MAX_STEPS = 64;

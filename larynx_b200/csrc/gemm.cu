@@ -46,13 +46,14 @@ bool pdl_enabled() {
   return env >= 0 ? env != 0 : t_pdl_auto;
 }
 
-int rows_per_block(int R) {
-  static int fixed = -1;
-  if (fixed < 0) {
+int rows_per_block(int R, int dflt) {
+  static int fixed = -2;
+  if (fixed == -2) {
     const char* e = getenv("LX_FLOW_ROWS_PER_BLOCK");
-    fixed = e ? atoi(e) : 8;
+    fixed = e ? atoi(e) : -1;
   }
-  if (fixed > 0) return fixed > 16 ? 16 : fixed;
+  const int v = fixed >= 0 ? fixed : dflt;
+  if (v > 0) return v > 16 ? 16 : v;
   // 0: up to 16, few enough that a small batch spreads over every SM in one wave
   const int per_sm = (R + num_sms() - 1) / num_sms();
   return per_sm < 1 ? 1 : per_sm > 16 ? 16 : per_sm;

@@ -39,9 +39,10 @@ void pdl_set_auto(bool on);
 // Batch plans of at most this many packed rows launch with PDL by default
 // (latency-bound: the single 20 s utterance is 2 x 1000 rows).
 constexpr int PDL_AUTO_MAX_ROWS = 16384;
-// Rows per block of the warp-per-row kernels (LX_FLOW_ROWS_PER_BLOCK, default
-// 8; 0 = as many as spread a small batch over every SM in one wave, <= 16).
-int rows_per_block(int R);
+// Rows per block of the warp-per-row kernels: LX_FLOW_ROWS_PER_BLOCK when set,
+// else `dflt` (the decode uses 8; the standalone ops 0); 0 = as many as
+// spread the rows over every SM in one wave, at most 16.
+int rows_per_block(int R, int dflt = 8);
 
 template <typename... KArgs, typename... Args>
 inline void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
@@ -75,6 +76,8 @@ bool tmap_f32(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, ui
 // Rows of the conv-pos A window (128 output rows + 30 taps, rounded to 8):
 // the box height of the conv's staging tensor maps.
 constexpr int CONV_WIN_ROWS = 160;
+
+constexpr int ROPE_MAX = 16384;  // positions covered by the rotary tables
 
 // Query rows per attention CTA.
 constexpr int ATT_Q_ROWS = 128;
