@@ -14,6 +14,7 @@ namespace {
 // previous kernel is still writing are read correctly after the wait, and
 // inputs it does not write arrive early.
 __device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+  if ((reinterpret_cast<uintptr_t>(p) & 15u) != 0 || (bytes & 15u) != 0) return;  // the bulk form's alignment rule
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
