@@ -68,6 +68,34 @@ def test_attention(lib, lengths, chunk):
     assert rel_l2(got[rows], ref_b) < 3e-3
 
 
+@pytest.mark.parametrize("step,chunk", [(0.26, 0), (0.26, 50), (1.0, 0), (-0.3, 0)])
+def test_attention_growing_row_max(lib, step, chunk):
+    """Scores that rise from one 128-key tile to the next, so that the row
+    maximum grows during the online softmax: by ~3 log2 units a tile
+    (step 0.26; half sums of p reach 2^9 while p itself stays below 2^8, the
+    exact pass of the softmax runs on every tile), by ~11.5 (step 1.0; every
+    tile rescales O) or falling (step -0.3; no tile after the first needs its
+    maximum)."""
+    lengths = [640, 300, 1000]
+    starts, R = packed_starts(lengths)
+    g = torch.Generator().manual_seed(17)
+    q = (1.0 + 0.05 * torch.randn(R, 1024, generator=g)).to(torch.bfloat16)
+    tile = torch.zeros(R)
+    for s, L in zip(starts, lengths):
+        tile[s:s + L] = torch.arange(L) // 128
+    k = ((step * tile)[:, None] + 0.05 * torch.randn(R, 1024, generator=g)).to(torch.bfloat16)
+    v = torch.randn(R, 1024, generator=g).to(torch.bfloat16)
+    out = torch.zeros(R, 1024, dtype=torch.bfloat16, device="cuda")
+    qd, kd, vd = q.cuda(), k.cuda(), v.cuda()
+    lib.op_attention(lengths, qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), out.data_ptr(), chunk)
+    torch.cuda.synchronize()
+    ref = attn_ref_fp64(q.double().numpy(), k.double().numpy(), v.double().numpy(), lengths, starts, chunk)
+    got = out.float().cpu().numpy()
+    assert np.isfinite(got).all()
+    rows = np.concatenate([np.arange(s, s + L) for s, L in zip(starts, lengths)])
+    assert rel_l2(got[rows], ref[rows]) < 4e-3
+
+
 def _ops_inputs(dtype_bf16, rows=2000, seed=1):
     g = torch.Generator().manual_seed(seed)
     x = torch.randn(rows, 1024, generator=g)
