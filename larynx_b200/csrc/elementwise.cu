@@ -49,8 +49,14 @@ __device__ __forceinline__ void store4(bf16* p, float4 v) {
 }
 
 // One warp per 1024-wide row; lane owns columns 4*lane + 128*i, i < 8.
-// Two-pass statistics in registers (mean, then centred variance), biased
-// variance, eps 1e-6, then (x - mean) * rstd * (1 + scale) + shift.
+// Biased variance, eps 1e-6, then (x - mean) * rstd * (1 + scale) + shift.
+// The decode's instance (PF = false) takes two-pass statistics in registers
+// (mean, then centred variance).  The standalone op instances (PF = true:
+// the row is prefetched into L2 before the dependency wait) take both sums
+// in one pass over x - K, K = the row's first element (the shifted-data
+// variance: var = E[(x-K)^2] - E[x-K]^2, whose cancellation is bounded by
+// (mean - K)^2 / var, small for a K drawn from the row), which saves one
+// warp reduction on the latency chain of a launch that moves ~12 MB.
 template <typename Tin, typename Tout, bool PF = false>
 __global__ void __launch_bounds__(512) k_adaln(const Tin* __restrict__ x, Tout* __restrict__ y,
                                                 const float* __restrict__ shift, const float* __restrict__ scale,
@@ -63,20 +69,41 @@ __global__ void __launch_bounds__(512) k_adaln(const Tin* __restrict__ x, Tout* 
   if (row >= R) return;
   const Tin* xr = x + static_cast<size_t>(row) * DIM;
   float4 v[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = load4(xr + 4 * lane + 128 * i);
   float s = 0.f;
+  if (!PF) {
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    v[i] = load4(xr + 4 * lane + 128 * i);
-    s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+    for (int i = 0; i < 8; ++i) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
   }
-  const float mean = warp_sum(s) * (1.0f / DIM);
-  float q = 0.f;
+  float mean, var;
+  if (PF) {
+    const float K = __shfl_sync(0xffffffffu, v[0].x, 0);
+    float s1 = 0.f, s2 = 0.f;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const float a = v[i].x - mean, b = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
-    q += (a * a + b * b) + (c * c + d * d);
+    for (int i = 0; i < 8; ++i) {
+      const float a = v[i].x - K, b = v[i].y - K, c = v[i].z - K, d = v[i].w - K;
+      s1 += (a + b) + (c + d);
+      s2 += (a * a + b * b) + (c * c + d * d);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+      s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+    }
+    const float m1 = s1 * (1.0f / DIM);
+    mean = K + m1;
+    var = fmaxf(s2 * (1.0f / DIM) - m1 * m1, 0.f);
+  } else {
+    mean = warp_sum(s) * (1.0f / DIM);
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float a = v[i].x - mean, b = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
+      q += (a * a + b * b) + (c * c + d * d);
+    }
+    var = warp_sum(q) * (1.0f / DIM);
   }
-  const float var = warp_sum(q) * (1.0f / DIM);
   const float rstd = 1.0f / sqrtf(var + 1e-6f);
   Tout* yr = y + static_cast<size_t>(row) * DIM;
 #pragma unroll
@@ -338,57 +365,94 @@ __global__ void k_gate_res(float* __restrict__ x, const Tin* __restrict__ y, con
   reinterpret_cast<float4*>(x)[i] = xv;
 }
 
-// Partial rotary of one row per warp: lanes 0..31 rotate pair i = lane of
-// channels (2i, 2i+1); every lane also copies its share of channels 64..1023.
+// Partial rotary of one row per warp: lanes 0..15 rotate the pairs of
+// channels 0..63 (lane l: pairs 2l, 2l+1), and every lane copies its share of
+// the other channels.  Before the dependency wait the row of x and the table
+// row of a speculative read of pos go into L2 (pos may still be being written
+// by the previous kernel: the speculative value, read at L2 with __ldcg so no
+// stale L1 line survives, only picks lines and the table address).  After the
+// wait the table row is loaded at that address while pos is read again; a
+// different pos reloads it.  The copies are stored first, the rotated chunk
+// last.  The table itself is never written by a kernel (it is uploaded once
+// by a blocking copy), so reading it early is safe.
 template <typename Tin>
 __global__ void __launch_bounds__(512) k_rotary(const Tin* __restrict__ x, float* __restrict__ y,
                                                  const int* __restrict__ pos, const float2* __restrict__ rope,
                                                  int R) {
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
-  // The table row of this row's position into L2 before the wait.  pos may
-  // still be being written by the previous kernel: the value read here only
-  // picks (clamped) lines to prefetch, and pos is read again after the wait.
-  // (Prefetching the row of x as well made this op slower: measured.)
-  if (row < R && lane == 0) {
-    int p = pos[row];
-    p = p < 0 ? 0 : (p >= ROPE_MAX ? ROPE_MAX - 1 : p);
-    prefetch_l2_bulk(rope + static_cast<size_t>(p) * 32, 32 * sizeof(float2));
+  int p_spec = 0;
+  if (row < R) {
+    const int p = __ldcg(pos + row);
+    p_spec = p < 0 ? 0 : (p >= ROPE_MAX ? ROPE_MAX - 1 : p);
+    if (lane == 0) {
+      prefetch_l2_bulk(x + static_cast<size_t>(row) * DIM, DIM * sizeof(Tin));
+      prefetch_l2_bulk(rope + static_cast<size_t>(p_spec) * 32, 32 * sizeof(float2));
+    }
   }
   pdl_wait();
   pdl_launch_dependents();  // after the wait: at most one dependent launch ahead
   if (row >= R) return;
   const Tin* xr = x + static_cast<size_t>(row) * DIM;
   float* yr = y + static_cast<size_t>(row) * DIM;
+  float4 v[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int c = 4 * lane + 128 * i;
-    float4 v = load4(xr + c);
-    if (c < HDIM) {
-      const float2* cs = rope + static_cast<size_t>(pos[row]) * 32 + (c >> 1);
-      const float2 t0 = __ldg(cs), t1 = __ldg(cs + 1);
-      const float a0 = v.x * t0.x - v.y * t0.y, a1 = v.y * t0.x + v.x * t0.y;
-      const float b0 = v.z * t1.x - v.w * t1.y, b1 = v.w * t1.x + v.z * t1.y;
-      v = make_float4(a0, a1, b0, b1);
-    }
-    store4(yr + c, v);
+  for (int i = 0; i < 8; ++i) v[i] = load4(xr + 4 * lane + 128 * i);
+  float2 t0 = make_float2(1.f, 0.f), t1 = make_float2(1.f, 0.f);
+  int p = p_spec;
+  if (lane < 16) {
+    p = pos[row];
+    const float2* cs = rope + static_cast<size_t>(p_spec) * 32 + 2 * lane;
+    t0 = __ldg(cs);
+    t1 = __ldg(cs + 1);
   }
+#pragma unroll
+  for (int i = 1; i < 8; ++i) store4(yr + 4 * lane + 128 * i, v[i]);
+  if (lane < 16) {
+    if (p != p_spec) {
+      const float2* cs = rope + static_cast<size_t>(p) * 32 + 2 * lane;
+      t0 = __ldg(cs);
+      t1 = __ldg(cs + 1);
+    }
+    const float4 w = v[0];
+    v[0] = make_float4(w.x * t0.x - w.y * t0.y, w.y * t0.x + w.x * t0.y, w.z * t1.x - w.w * t1.y,
+                       w.w * t1.x + w.z * t1.y);
+  }
+  store4(yr + 4 * lane, v[0]);
 }
 
+// Two float4 per thread (block b covers 512 consecutive float4): one wave of
+// ~7 blocks per SM at [2000, 1024], against two waves for one float4 per
+// thread (measured: 0.88 / 0.78 vs 0.73 / 0.60 of HBM, fp32 / bf16 in).
+constexpr int GELU_PER_THREAD = 2;
 template <typename Tin>
-__global__ void k_gelu(const Tin* __restrict__ x, float* __restrict__ y, size_t n4) {
-  const size_t b0 = static_cast<size_t>(blockIdx.x) * blockDim.x;
-  if (threadIdx.x == 0 && b0 + blockDim.x <= n4) prefetch_l2_bulk(x + b0 * 4, blockDim.x * 4 * sizeof(Tin));
+__global__ void __launch_bounds__(256) k_gelu(const Tin* __restrict__ x, float* __restrict__ y, size_t n4) {
+  const size_t b0 = static_cast<size_t>(blockIdx.x) * blockDim.x * GELU_PER_THREAD;
+  if (threadIdx.x == 0) {
+    const size_t span = static_cast<size_t>(blockDim.x) * GELU_PER_THREAD;
+    const size_t cnt = n4 - b0 < span ? n4 - b0 : span;
+    prefetch_l2_bulk(x + b0 * 4, static_cast<uint32_t>(cnt * 4 * sizeof(Tin)));
+  }
   pdl_wait();
   pdl_launch_dependents();  // after the wait: at most one dependent launch ahead
-  const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i >= n4) return;
-  float4 v = load4(x + i * 4);
-  v.x = gelu_tanh_fast(v.x);
-  v.y = gelu_tanh_fast(v.y);
-  v.z = gelu_tanh_fast(v.z);
-  v.w = gelu_tanh_fast(v.w);
-  reinterpret_cast<float4*>(y)[i] = v;
+  float4 v[GELU_PER_THREAD];
+#pragma unroll
+  for (int u = 0; u < GELU_PER_THREAD; ++u) {
+    const size_t i = b0 + threadIdx.x + static_cast<size_t>(u) * blockDim.x;
+    if (i < n4) v[u] = load4(x + i * 4);
+  }
+#pragma unroll
+  for (int u = 0; u < GELU_PER_THREAD; ++u) {
+    const size_t i = b0 + threadIdx.x + static_cast<size_t>(u) * blockDim.x;
+    if (i < n4) {
+      float4 w = v[u];
+      w.x = gelu_tanh_fast(w.x);
+      w.y = gelu_tanh_fast(w.y);
+      w.z = gelu_tanh_fast(w.z);
+      w.w = gelu_tanh_fast(w.w);
+      reinterpret_cast<float4*>(y)[i] = w;
+    }
+  }
 }
 
 inline unsigned blocks_for(size_t n, unsigned t) { return static_cast<unsigned>((n + t - 1) / t); }
@@ -483,10 +547,10 @@ void op_rotary_bf16(const bf16* x, float* y, const int* pos, const float2* rope,
   if (R > 0) launch_pdl(k_rotary<bf16>, dim3((R + rows_per_block(R, 0) - 1) / rows_per_block(R, 0)), dim3(32 * rows_per_block(R, 0)), 0, s, x, y, pos, rope, R);
 }
 void op_gelu_f32(const float* x, float* y, size_t n, cudaStream_t s) {
-  if (n >= 4) launch_pdl(k_gelu<float>, dim3(blocks_for(n / 4, 256)), dim3(256), 0, s, x, y, n / 4);
+  if (n >= 4) launch_pdl(k_gelu<float>, dim3(blocks_for(n / 4, 256 * GELU_PER_THREAD)), dim3(256), 0, s, x, y, n / 4);
 }
 void op_gelu_bf16(const bf16* x, float* y, size_t n, cudaStream_t s) {
-  if (n >= 4) launch_pdl(k_gelu<bf16>, dim3(blocks_for(n / 4, 256)), dim3(256), 0, s, x, y, n / 4);
+  if (n >= 4) launch_pdl(k_gelu<bf16>, dim3(blocks_for(n / 4, 256 * GELU_PER_THREAD)), dim3(256), 0, s, x, y, n / 4);
 }
 
 }  // namespace lx
