@@ -431,8 +431,8 @@ void conv_pos(const CUtensorMap& A, const CUtensorMap& B, int Ms, const float* b
     cudaFuncSetAttribute(k_conv_win<EpiConv>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     attr_done[dev & 63] = true;
   }
-  const int tiles = ((Ms + GEMM_BM - 1) / GEMM_BM) * (DIM / 64);
-  const int grid = tiles < num_sms() ? tiles : num_sms();
+  const int items = ((Ms + CONV_ROWT * GEMM_BM - 1) / (CONV_ROWT * GEMM_BM)) * (DIM / 64);
+  const int grid = items < num_sms() ? items : num_sms();
   if (grid <= 0) return;
   GemmShape sh{Ms, DIM, 0, 0, err};
   launch_pdl(k_conv_win<EpiConv>, dim3(grid), dim3(CONV_THREADS), smem, s, A, B, sh, e);

@@ -277,14 +277,21 @@ __global__ void __launch_bounds__(gemm_threads(MODE), 1)
 // operand is the window's descriptor advanced by kb rows (kb x 128 bytes).
 // The per-tap [64 out x 64 in] weight slices stream through their own ring.
 // A traffic per tile: 20 KB instead of 31 x 16 KB.
-//   warp 0      TMA: A window (2 slots), weight slices (CONV_BSTAGES slots)
+// A work item is CONV_ROWT consecutive tiles of one group: each weight slice
+// feeds CONV_ROWT x 4 MMAs per barrier wait (a wait on an mbarrier costs about
+// as long as the four N = 64 MMAs of one tile, which left the tensor pipe
+// three quarters idle with one tile per item) and is read from L2 half as often.
+//   warp 0      TMA: A windows (2 slots x CONV_ROWT), weight slices (CONV_BSTAGES slots)
 //   warp 1      TMEM allocator; lane 0 issues tcgen05.mma (M=128, N=64, K=16)
 //   warps 2..17 epilogue, four per TMEM lane quarter, 16 columns each
 // ---------------------------------------------------------------------------
 constexpr int CONV_WIN_BYTES = CONV_WIN_ROWS * 128;
+constexpr int CONV_ROWT = 2;  // 128-row tiles per work item, sharing each weight slice
 constexpr int CONV_BSTAGES = 12;
 constexpr int CONV_THREADS = 64 + 16 * 32;
-constexpr int conv_win_smem_bytes() { return 1024 + 2 * CONV_WIN_BYTES + CONV_BSTAGES * 64 * 128 + 512; }
+constexpr int conv_win_smem_bytes() {
+  return 1024 + 2 * CONV_ROWT * CONV_WIN_BYTES + CONV_BSTAGES * 64 * 128 + 512;
+}
 
 template <class Epi>
 __global__ void __launch_bounds__(CONV_THREADS, 1)
@@ -292,12 +299,15 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
                Epi epi) {
   constexpr int BN = 64;
   constexpr int B_BYTES = 64 * 128;
-  constexpr uint32_t TMEM_COLS = 128;  // two 64-column accumulators
+  constexpr int ACC_COLS = CONV_ROWT * BN;          // one accumulator set: CONV_ROWT tiles of 64 columns
+  // two sets, double-buffered against the epilogue (allocated as a power of two)
+  constexpr uint32_t TMEM_COLS = 2 * ACC_COLS <= 256 ? 256 : 512;
+  static_assert(2 * ACC_COLS <= 512, "two accumulator sets fit in tensor memory");
   constexpr uint32_t IDESC = idesc_bf16_f32(GEMM_BM, BN);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sA = smem;
-  uint8_t* sB = smem + 2 * CONV_WIN_BYTES;
+  uint8_t* sA = smem;  // 2 slots x CONV_ROWT windows
+  uint8_t* sB = smem + 2 * CONV_ROWT * CONV_WIN_BYTES;
   uint64_t* a_full = reinterpret_cast<uint64_t*>(sB + CONV_BSTAGES * B_BYTES);
   uint64_t* a_empty = a_full + 2;
   uint64_t* full = a_empty + 2;
@@ -338,20 +348,26 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
   pdl_launch_dependents();
   pdl_wait();
 
+  constexpr int ITEM_ROWS = CONV_ROWT * GEMM_BM;
   const int tiles_n = sh.N / BN;
-  const int n_tiles = ((sh.M + GEMM_BM - 1) / GEMM_BM) * tiles_n;
+  const int n_items = ((sh.M + ITEM_ROWS - 1) / ITEM_ROWS) * tiles_n;
 
   if (warp == 0) {
     if (lane == 0) {
       int as = 0, bs = 0;
       uint32_t aph = 0, bph = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
-        const int m0 = (tile / tiles_n) * GEMM_BM;
-        const int n0 = (tile % tiles_n) * BN;  // group g = n0 / 64
+      for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x) {
+        const int m0 = (item / tiles_n) * ITEM_ROWS;
+        const int n0 = (item % tiles_n) * BN;  // group g = n0 / 64
         if (!(ok = mbar_wait(&a_empty[as], aph ^ 1u, sh.err, abort_flag, DEV_TIMEOUT_PRODUCER))) break;
-        mbar_arrive_expect_tx(&a_full[as], CONV_WIN_BYTES);
-        tma_load_2d(sA + as * CONV_WIN_BYTES, &tmA, &a_full[as], n0, m0 - (CONV_TAPS - 1));
+        // a tile wholly past the last row is not loaded: its accumulator rows
+        // are never stored
+        const int nt = min(CONV_ROWT, (sh.M - m0 + GEMM_BM - 1) / GEMM_BM);
+        mbar_arrive_expect_tx(&a_full[as], static_cast<uint32_t>(nt * CONV_WIN_BYTES));
+        for (int r = 0; r < nt; ++r)
+          tma_load_2d(sA + (as * CONV_ROWT + r) * CONV_WIN_BYTES, &tmA, &a_full[as], n0,
+                      m0 + r * GEMM_BM - (CONV_TAPS - 1));
         if (++as == 2) {
           as = 0;
           aph ^= 1u;
@@ -372,20 +388,25 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
       int as = 0, bs = 0, acc = 0;
       uint32_t aph = 0, bph = 0, acc_phase = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
+      for (int item = blockIdx.x; ok && item < n_items; item += gridDim.x) {
         if (!(ok = mbar_wait(&tempty[acc], acc_phase ^ 1u, sh.err, abort_flag, DEV_TIMEOUT_MMA))) break;
         if (!(ok = mbar_wait(&a_full[as], aph, sh.err, abort_flag, DEV_TIMEOUT_MMA))) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-        const uint32_t wa = smem_u32(sA + as * CONV_WIN_BYTES);
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * ACC_COLS);
+        const uint32_t wa = smem_u32(sA + as * CONV_ROWT * CONV_WIN_BYTES);
         for (int kb = 0; kb < CONV_TAPS; ++kb) {
           if (!(ok = mbar_wait(&full[bs], bph, sh.err, abort_flag, DEV_TIMEOUT_MMA))) break;
           tc_fence_after();
-          const uint64_t da = sdesc_sw128(wa + static_cast<uint32_t>(kb) * 128u);
           const uint64_t db = sdesc_sw128(smem_u32(sB + bs * B_BYTES));
 #pragma unroll
-          for (int k = 0; k < GEMM_BK / 16; ++k)
-            umma_ss(d_tmem, da + 2 * k, db + 2 * k, IDESC, (kb > 0 || k > 0) ? 1u : 0u);
+          for (int r = 0; r < CONV_ROWT; ++r) {
+            const uint64_t da =
+                sdesc_sw128(wa + static_cast<uint32_t>(r * CONV_WIN_BYTES) + static_cast<uint32_t>(kb) * 128u);
+#pragma unroll
+            for (int k = 0; k < GEMM_BK / 16; ++k)
+              umma_ss(d_tmem + static_cast<uint32_t>(r * BN), da + 2 * k, db + 2 * k, IDESC,
+                      (kb > 0 || k > 0) ? 1u : 0u);
+          }
           umma_commit(&empty[bs]);
           if (++bs == CONV_BSTAGES) {
             bs = 0;
@@ -408,18 +429,21 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
     const int c0 = ((warp - 2) >> 2) * 16;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
-      const int m0 = (tile / tiles_n) * GEMM_BM;
-      const int n0 = (tile % tiles_n) * BN;
+    for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+      const int m0 = (item / tiles_n) * ITEM_ROWS;
+      const int n0 = (item % tiles_n) * BN;
       const bool ok = mbar_wait(&tfull[acc], acc_phase, sh.err, abort_flag, DEV_TIMEOUT_EPILOGUE);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
       const int rt = q * 32 + lane;
-      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
-      float va[16];
-      tmem_ld16(t_row + c0, va);
-      tmem_ld_wait();
-      epi_chunk<false>(epi, nullptr, rt, m0 + rt, n0, c0, sh, va);
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * ACC_COLS);
+#pragma unroll
+      for (int r = 0; r < CONV_ROWT; ++r) {
+        float va[16];
+        tmem_ld16(t_row + static_cast<uint32_t>(r * BN) + c0, va);
+        tmem_ld_wait();
+        epi_chunk<false>(epi, nullptr, rt, m0 + r * GEMM_BM + rt, n0, c0, sh, va);
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
