@@ -280,14 +280,16 @@ __global__ void __launch_bounds__(gemm_threads(MODE), 1)
 // A work item is CONV_ROWT consecutive tiles of one group: each weight slice
 // feeds CONV_ROWT x 4 MMAs per barrier wait (a wait on an mbarrier costs about
 // as long as the four N = 64 MMAs of one tile, which left the tensor pipe
-// three quarters idle with one tile per item) and is read from L2 half as often.
+// three quarters idle with one tile per item) and is read from L2 CONV_ROWT
+// times less often.  Measured per decode: 18.8 ms (one tile), 14.2 (two),
+// 12.8 (three), 12.2 (four; the weight ring shrinks to 6 slots to fit).
 //   warp 0      TMA: A windows (2 slots x CONV_ROWT), weight slices (CONV_BSTAGES slots)
 //   warp 1      TMEM allocator; lane 0 issues tcgen05.mma (M=128, N=64, K=16)
 //   warps 2..17 epilogue, four per TMEM lane quarter, 16 columns each
 // ---------------------------------------------------------------------------
 constexpr int CONV_WIN_BYTES = CONV_WIN_ROWS * 128;
-constexpr int CONV_ROWT = 2;  // 128-row tiles per work item, sharing each weight slice
-constexpr int CONV_BSTAGES = 12;
+constexpr int CONV_ROWT = 4;  // 128-row tiles per work item, sharing each weight slice
+constexpr int CONV_BSTAGES = 6;
 constexpr int CONV_THREADS = 64 + 16 * 32;
 constexpr int conv_win_smem_bytes() {
   return 1024 + 2 * CONV_ROWT * CONV_WIN_BYTES + CONV_BSTAGES * 64 * 128 + 512;
