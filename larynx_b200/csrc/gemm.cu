@@ -420,22 +420,57 @@ void gemm_in_proj(int bn, const CUtensorMap& A, const CUtensorMap& B, int M, con
   launch_bn(bn, A, B, M, DIM, MEL, 0, e, err, s);
 }
 
-void conv_pos(const CUtensorMap& A, const CUtensorMap& B, int Ms, const float* bias, int second, bf16* out_stage,
-              float* x, const int* s2p, int* err, cudaStream_t s) {
-  EpiConv e{bias, second, out_stage, x, s2p};
-  constexpr int smem = conv_win_smem_bytes();
+namespace {
+template <int ROWT>
+void launch_conv(const CUtensorMap& A, const CUtensorMap& B, const GemmShape& sh, const EpiConv& e, int items,
+                 cudaStream_t s) {
+  constexpr int smem = conv_win_smem_bytes(ROWT);
   static bool attr_done[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr_done[dev & 63]) {
-    cudaFuncSetAttribute(k_conv_win<EpiConv>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaFuncSetAttribute(k_conv_win<ROWT, EpiConv>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     attr_done[dev & 63] = true;
   }
-  const int items = ((Ms + CONV_ROWT * GEMM_BM - 1) / (CONV_ROWT * GEMM_BM)) * (DIM / 64);
   const int grid = items < num_sms() ? items : num_sms();
-  if (grid <= 0) return;
+  launch_pdl(k_conv_win<ROWT, EpiConv>, dim3(grid), dim3(CONV_THREADS), smem, s, A, B, sh, e);
+}
+}  // namespace
+
+// Row tiles per conv work item: the fewest waves of items, each weighted by
+// the measured time of an item of ROWT tiles relative to ROWT one-tile items
+// (1, 0.755, 0.65 per tile at 1, 2, 4 tiles on the config-3 decode).
+static int conv_rowt(int Ms) {
+  static const int rowts[3] = {1, 2, 4};
+  static const double per_tile[3] = {1.0, 0.755, 0.65};
+  int best = 1;
+  double best_t = 1e300;
+  for (int i = 0; i < 3; ++i) {
+    const int rt = rowts[i];
+    const long items = static_cast<long>((Ms + rt * GEMM_BM - 1) / (rt * GEMM_BM)) * (DIM / 64);
+    const long waves = (items + num_sms() - 1) / num_sms();
+    const double t = static_cast<double>(waves) * rt * per_tile[i];
+    if (t < best_t - 1e-9) {
+      best_t = t;
+      best = rt;
+    }
+  }
+  return best;
+}
+
+void conv_pos(const CUtensorMap& A, const CUtensorMap& B, int Ms, const float* bias, int second, bf16* out_stage,
+              float* x, const int* s2p, int* err, cudaStream_t s) {
+  if (Ms <= 0) return;
+  EpiConv e{bias, second, out_stage, x, s2p};
   GemmShape sh{Ms, DIM, 0, 0, err};
-  launch_pdl(k_conv_win<EpiConv>, dim3(grid), dim3(CONV_THREADS), smem, s, A, B, sh, e);
+  const int rt = conv_rowt(Ms);
+  const int items = ((Ms + rt * GEMM_BM - 1) / (rt * GEMM_BM)) * (DIM / 64);
+  if (rt == 4)
+    launch_conv<4>(A, B, sh, e, items, s);
+  else if (rt == 2)
+    launch_conv<2>(A, B, sh, e, items, s);
+  else
+    launch_conv<1>(A, B, sh, e, items, s);
 }
 
 }  // namespace lx

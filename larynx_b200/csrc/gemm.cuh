@@ -277,44 +277,47 @@ __global__ void __launch_bounds__(gemm_threads(MODE), 1)
 // operand is the window's descriptor advanced by kb rows (kb x 128 bytes).
 // The per-tap [64 out x 64 in] weight slices stream through their own ring.
 // A traffic per tile: 20 KB instead of 31 x 16 KB.
-// A work item is CONV_ROWT consecutive tiles of one group: each weight slice
-// feeds CONV_ROWT x 4 MMAs per barrier wait (a wait on an mbarrier costs about
-// as long as the four N = 64 MMAs of one tile, which left the tensor pipe
-// three quarters idle with one tile per item) and is read from L2 CONV_ROWT
-// times less often.  Measured per decode: 18.8 ms (one tile), 14.2 (two),
-// 12.8 (three), 12.2 (four; the weight ring shrinks to 6 slots to fit).
-//   warp 0      TMA: A windows (2 slots x CONV_ROWT), weight slices (CONV_BSTAGES slots)
+// A work item is ROWT consecutive tiles of one group: each weight slice feeds
+// ROWT x 4 MMAs per barrier wait (a wait on an mbarrier costs about as long as
+// the four N = 64 MMAs of one tile, which left the tensor pipe three quarters
+// idle with one tile per item) and is read from L2 ROWT times less often.
+// Measured on the config-3 decode: 18.8 ms (one tile), 14.2 (two), 12.8
+// (three), 12.2 (four).  Fewer, longer items fill fewer SMs, so the host picks
+// ROWT per launch from the row count (conv_pos, gemm.cu).
+//   warp 0      TMA: A windows (2 slots x ROWT), weight slices (conv_bstages slots)
 //   warp 1      TMEM allocator; lane 0 issues tcgen05.mma (M=128, N=64, K=16)
 //   warps 2..17 epilogue, four per TMEM lane quarter, 16 columns each
 // ---------------------------------------------------------------------------
 constexpr int CONV_WIN_BYTES = CONV_WIN_ROWS * 128;
-constexpr int CONV_ROWT = 4;  // 128-row tiles per work item, sharing each weight slice
-constexpr int CONV_BSTAGES = 6;
+// ROWT = 128-row tiles per work item (1, 2 or 4), sharing each weight slice;
+// the weight ring shrinks at 4 so that four pairs of windows fit.
+__host__ __device__ constexpr int conv_bstages(int rowt) { return rowt >= 4 ? 6 : 12; }
 constexpr int CONV_THREADS = 64 + 16 * 32;
-constexpr int conv_win_smem_bytes() {
-  return 1024 + 2 * CONV_ROWT * CONV_WIN_BYTES + CONV_BSTAGES * 64 * 128 + 512;
+__host__ __device__ constexpr int conv_win_smem_bytes(int rowt) {
+  return 1024 + 2 * rowt * CONV_WIN_BYTES + conv_bstages(rowt) * 64 * 128 + 512;
 }
 
-template <class Epi>
+template <int ROWT, class Epi>
 __global__ void __launch_bounds__(CONV_THREADS, 1)
     k_conv_win(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmShape sh,
                Epi epi) {
   constexpr int BN = 64;
   constexpr int B_BYTES = 64 * 128;
-  constexpr int ACC_COLS = CONV_ROWT * BN;          // one accumulator set: CONV_ROWT tiles of 64 columns
+  constexpr int BSTAGES = conv_bstages(ROWT);
+  constexpr int ACC_COLS = ROWT * BN;          // one accumulator set: ROWT tiles of 64 columns
   // two sets, double-buffered against the epilogue (allocated as a power of two)
   constexpr uint32_t TMEM_COLS = 2 * ACC_COLS <= 256 ? 256 : 512;
   static_assert(2 * ACC_COLS <= 512, "two accumulator sets fit in tensor memory");
   constexpr uint32_t IDESC = idesc_bf16_f32(GEMM_BM, BN);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sA = smem;  // 2 slots x CONV_ROWT windows
-  uint8_t* sB = smem + 2 * CONV_ROWT * CONV_WIN_BYTES;
-  uint64_t* a_full = reinterpret_cast<uint64_t*>(sB + CONV_BSTAGES * B_BYTES);
+  uint8_t* sA = smem;  // 2 slots x ROWT windows
+  uint8_t* sB = smem + 2 * ROWT * CONV_WIN_BYTES;
+  uint64_t* a_full = reinterpret_cast<uint64_t*>(sB + BSTAGES * B_BYTES);
   uint64_t* a_empty = a_full + 2;
   uint64_t* full = a_empty + 2;
-  uint64_t* empty = full + CONV_BSTAGES;
-  uint64_t* tfull = empty + CONV_BSTAGES;
+  uint64_t* empty = full + BSTAGES;
+  uint64_t* tfull = empty + BSTAGES;
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -328,7 +331,7 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
       mbar_init(&tfull[i], 1);
       mbar_init(&tempty[i], 16);
     }
-    for (int i = 0; i < CONV_BSTAGES; ++i) {
+    for (int i = 0; i < BSTAGES; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1);
     }
@@ -350,7 +353,7 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
   pdl_launch_dependents();
   pdl_wait();
 
-  constexpr int ITEM_ROWS = CONV_ROWT * GEMM_BM;
+  constexpr int ITEM_ROWS = ROWT * GEMM_BM;
   const int tiles_n = sh.N / BN;
   const int n_items = ((sh.M + ITEM_ROWS - 1) / ITEM_ROWS) * tiles_n;
 
@@ -365,10 +368,10 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
         if (!(ok = mbar_wait(&a_empty[as], aph ^ 1u, sh.err, abort_flag, DEV_TIMEOUT_PRODUCER))) break;
         // a tile wholly past the last row is not loaded: its accumulator rows
         // are never stored
-        const int nt = min(CONV_ROWT, (sh.M - m0 + GEMM_BM - 1) / GEMM_BM);
+        const int nt = min(ROWT, (sh.M - m0 + GEMM_BM - 1) / GEMM_BM);
         mbar_arrive_expect_tx(&a_full[as], static_cast<uint32_t>(nt * CONV_WIN_BYTES));
         for (int r = 0; r < nt; ++r)
-          tma_load_2d(sA + (as * CONV_ROWT + r) * CONV_WIN_BYTES, &tmA, &a_full[as], n0,
+          tma_load_2d(sA + (as * ROWT + r) * CONV_WIN_BYTES, &tmA, &a_full[as], n0,
                       m0 + r * GEMM_BM - (CONV_TAPS - 1));
         if (++as == 2) {
           as = 0;
@@ -378,7 +381,7 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
           if (!(ok = mbar_wait(&empty[bs], bph ^ 1u, sh.err, abort_flag, DEV_TIMEOUT_PRODUCER))) break;
           mbar_arrive_expect_tx(&full[bs], B_BYTES);
           tma_load_2d(sB + bs * B_BYTES, &tmB, &full[bs], 0, sh.b_off + ((n0 / 64) * CONV_TAPS + kb) * 64);
-          if (++bs == CONV_BSTAGES) {
+          if (++bs == BSTAGES) {
             bs = 0;
             bph ^= 1u;
           }
@@ -395,13 +398,13 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
         if (!(ok = mbar_wait(&a_full[as], aph, sh.err, abort_flag, DEV_TIMEOUT_MMA))) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * ACC_COLS);
-        const uint32_t wa = smem_u32(sA + as * CONV_ROWT * CONV_WIN_BYTES);
+        const uint32_t wa = smem_u32(sA + as * ROWT * CONV_WIN_BYTES);
         for (int kb = 0; kb < CONV_TAPS; ++kb) {
           if (!(ok = mbar_wait(&full[bs], bph, sh.err, abort_flag, DEV_TIMEOUT_MMA))) break;
           tc_fence_after();
           const uint64_t db = sdesc_sw128(smem_u32(sB + bs * B_BYTES));
 #pragma unroll
-          for (int r = 0; r < CONV_ROWT; ++r) {
+          for (int r = 0; r < ROWT; ++r) {
             const uint64_t da =
                 sdesc_sw128(wa + static_cast<uint32_t>(r * CONV_WIN_BYTES) + static_cast<uint32_t>(kb) * 128u);
 #pragma unroll
@@ -410,7 +413,7 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
                       (kb > 0 || k > 0) ? 1u : 0u);
           }
           umma_commit(&empty[bs]);
-          if (++bs == CONV_BSTAGES) {
+          if (++bs == BSTAGES) {
             bs = 0;
             bph ^= 1u;
           }
@@ -440,7 +443,7 @@ __global__ void __launch_bounds__(CONV_THREADS, 1)
       const int rt = q * 32 + lane;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * ACC_COLS);
 #pragma unroll
-      for (int r = 0; r < CONV_ROWT; ++r) {
+      for (int r = 0; r < ROWT; ++r) {
         float va[16];
         tmem_ld16(t_row + static_cast<uint32_t>(r * BN) + c0, va);
         tmem_ld_wait();
