@@ -29,7 +29,6 @@ enum GemmMode : int { MODE_GEMM = 0, MODE_RESID = 2 };
 
 constexpr int GEMM_BM = 128;
 constexpr int GEMM_BK = 64;
-constexpr int GEMM_THREADS = 192;
 constexpr int CONV_TAPS = 31;
 
 struct GemmShape {
@@ -42,7 +41,12 @@ __host__ __device__ constexpr int tmem_cols_for(int bn) {
   return (2 * bn) <= 32 ? 32 : (2 * bn) <= 64 ? 64 : (2 * bn) <= 128 ? 128 : (2 * bn) <= 256 ? 256 : 512;
 }
 
-__host__ __device__ constexpr int gemm_threads(int mode) { return mode == MODE_RESID ? 224 : GEMM_THREADS; }
+// Epilogue warps: MODE_GEMM has eight (two per TMEM lane quarter, one per
+// column half of the tile), so twice the rows' global traffic is in flight
+// for epilogue-bound shapes (the K = 80 input projection, small batches);
+// MODE_RESID has four beside its residual loader.
+__host__ __device__ constexpr int gemm_epi_warps(int mode) { return mode == MODE_RESID ? 4 : 8; }
+__host__ __device__ constexpr int gemm_threads(int mode) { return mode == MODE_RESID ? 224 : 64 + 32 * 8; }
 
 template <int BN, int STAGES, int MODE = MODE_GEMM>
 __host__ __device__ constexpr int gemm_smem_bytes() {
@@ -113,7 +117,7 @@ __global__ void __launch_bounds__(gemm_threads(MODE), 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 4);
+      mbar_init(&tempty[a], gemm_epi_warps(MODE));
     }
     mbar_init(x_full, 1);
     mbar_init(x_empty, 4);
@@ -217,8 +221,16 @@ __global__ void __launch_bounds__(gemm_threads(MODE), 1)
       }
     }
   } else {
-    // epilogue warps 2..5 -> TMEM lane quarters 2,3,0,1
+    // epilogue warps 2.. -> TMEM lane quarters 2,3,0,1(,2,3,0,1); with eight
+    // warps the second four take the right half of the tile's columns
+    // (a BN whose half is not a multiple of 16 leaves the whole tile to the
+    // first four, and the second four only keep the barrier protocol)
+    constexpr bool SPLIT = gemm_epi_warps(MODE) == 8 && (BN / 2) % 16 == 0;
+    constexpr int EPI_COLS = SPLIT ? BN / 2 : BN;
     const int q = warp & 3;
+    const int grp = (warp - 2) >> 2;
+    const int cb = grp * EPI_COLS;
+    const bool has_cols = SPLIT || grp == 0;
     int acc = 0;
     uint32_t acc_phase = 0;
     uint32_t xph = 0;
@@ -231,20 +243,23 @@ __global__ void __launch_bounds__(gemm_threads(MODE), 1)
       tc_fence_after();
       const int rt = q * 32 + lane;  // row inside the tile
       const int row = m0 + rt;
-      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      const uint32_t t_row =
+          tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN + cb);
       // software-pipelined: the TMEM load of chunk c+1 is in flight while
       // chunk c is processed (tcgen05.wait::ld waits for all of this thread's loads)
       float va[16], vb[16];
-      tmem_ld16(t_row, va);
-      tmem_ld_wait();
-#pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
-        if (c0 + 16 < BN) tmem_ld16(t_row + c0 + 16, vb);
-        epi_chunk<RES>(epi, sX, rt, row, n0, c0, sh, va);
+      if (has_cols) {
+        tmem_ld16(t_row, va);
         tmem_ld_wait();
-        if (c0 + 16 >= BN) break;
-        if (c0 + 32 < BN) tmem_ld16(t_row + c0 + 32, va);
-        epi_chunk<RES>(epi, sX, rt, row, n0, c0 + 16, sh, vb);
+      }
+#pragma unroll 1
+      for (int c0 = 0; has_cols && c0 < EPI_COLS; c0 += 32) {
+        if (c0 + 16 < EPI_COLS) tmem_ld16(t_row + c0 + 16, vb);
+        epi_chunk<RES>(epi, sX, rt, row, n0, cb + c0, sh, va);
+        tmem_ld_wait();
+        if (c0 + 16 >= EPI_COLS) break;
+        if (c0 + 32 < EPI_COLS) tmem_ld16(t_row + c0 + 32, va);
+        epi_chunk<RES>(epi, sX, rt, row, n0, cb + c0 + 16, sh, vb);
         tmem_ld_wait();
       }
       tc_fence_before();
