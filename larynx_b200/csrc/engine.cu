@@ -523,6 +523,7 @@ int ensure_workspace(lx_flow* h, const Plan& p, size_t in_floats, int n_utt) {
     ok &= tmap_bf16(&w.tm_k, w.k, R, DIM, DIM, 128, 64);
     ok &= tmap_bf16(&w.tm_v, w.v, R, DIM, DIM, 128, 64);
     ok &= tmap_f32(&w.tm_x, w.x, R, DIM, DIM, 128, 32);
+    ok &= tmap_f32(&w.tm_xs, w.x, R, DIM, DIM, 32, 32);
     if (!ok) return h->fail(LX_ERR_CUDA, "cuTensorMapEncodeTiled failed for a workspace tensor");
     ++w.generation;
   }
@@ -614,7 +615,7 @@ void enqueue_dit(lx_flow* h, const Plan& p, const float* mod, const float* mod_f
           [&] { attention(w.tm_q, w.tm_k, w.tm_v, w.tiles, static_cast<int>(p.tiles.size()), chunk, w.ao, err, s); });
     timed(h, K_OUT, s, [&] {
       if (pair_d)
-        gemm_pair_gate_res(w.tm_ao, W.tm_wo[0], w.tm_x, R, DIM, l * DIM, W.bo + static_cast<size_t>(l) * DIM,
+        gemm_pair_gate_res(w.tm_ao, W.tm_wo[0], w.tm_x, w.tm_xs, R, DIM, l * DIM, W.bo + static_cast<size_t>(l) * DIM,
                            m + 2 * DIM, w.x, err, s);
       else
         gemm_gate_res_tma(w.tm_ao, W.tm_wo[0], w.tm_x, R, DIM, l * DIM, W.bo + static_cast<size_t>(l) * DIM,
@@ -629,7 +630,7 @@ void enqueue_dit(lx_flow* h, const Plan& p, const float* mod, const float* mod_f
     });
     timed(h, K_FF2, s, [&] {
       if (pair_d)
-        gemm_pair_gate_res(w.tm_h, W.tm_w2[0], w.tm_x, R, FF, l * DIM, W.b2 + static_cast<size_t>(l) * DIM,
+        gemm_pair_gate_res(w.tm_h, W.tm_w2[0], w.tm_x, w.tm_xs, R, FF, l * DIM, W.b2 + static_cast<size_t>(l) * DIM,
                            m + 5 * DIM, w.x, err, s);
       else
         gemm_gate_res_tma(w.tm_h, W.tm_w2[0], w.tm_x, R, FF, l * DIM, W.b2 + static_cast<size_t>(l) * DIM,

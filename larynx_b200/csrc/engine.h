@@ -84,7 +84,8 @@ struct Workspace {
   float* cap = nullptr;  // capture scratch [R][1024]
   size_t capCap = 0;
   CUtensorMap tm_xn, tm_ao, tm_h, tm_xb, tm_acond, tm_stage1, tm_stage2, tm_q, tm_k, tm_v;
-  CUtensorMap tm_x;  // fp32 residual stream, box 128 x 32
+  CUtensorMap tm_x;   // fp32 residual stream, box 128 x 32
+  CUtensorMap tm_xs;  // the same, box 32 x 32 (TMA stores of the residual GEMM epilogue)
   uint64_t generation = 0;
 };
 

@@ -196,6 +196,21 @@ struct EpiGateResSmem {
   const float* bias;
   const float* gate;
   float* x;
+  // o = xin + gate * (v + bias), the stored value, without the store (the
+  // pair kernel writes it back into the residual box and stores it by TMA)
+  __device__ __forceinline__ void apply(int col0, const float (&v)[16], const float (&xin)[16], float (&o)[16]) const {
+    const float4* b4 = reinterpret_cast<const float4*>(bias + col0);
+    const float4* g4 = reinterpret_cast<const float4*>(gate + col0);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float4 b = __ldg(b4 + j);
+      const float4 g = __ldg(g4 + j);
+      o[4 * j + 0] = xin[4 * j + 0] + g.x * (v[4 * j + 0] + b.x);
+      o[4 * j + 1] = xin[4 * j + 1] + g.y * (v[4 * j + 1] + b.y);
+      o[4 * j + 2] = xin[4 * j + 2] + g.z * (v[4 * j + 2] + b.z);
+      o[4 * j + 3] = xin[4 * j + 3] + g.w * (v[4 * j + 3] + b.w);
+    }
+  }
   __device__ __forceinline__ void operator()(int row, int col0, float (&v)[16], const float (&xin)[16]) const {
     const float4* b4 = reinterpret_cast<const float4*>(bias + col0);
     const float4* g4 = reinterpret_cast<const float4*>(gate + col0);
@@ -310,7 +325,7 @@ static void launch(const CUtensorMap& A, const CUtensorMap& B, int M, int N, int
 // CTA-pair launch: persistent grid of up to num_sms() / 2 clusters of 2.
 template <int STAGES, bool RES, int XS, class Epi>
 static void launch_pair(const CUtensorMap& A, const CUtensorMap& B, int M, int N, int K, int b_off, const Epi& epi,
-                        int* err, cudaStream_t s, const CUtensorMap* X = nullptr) {
+                        int* err, cudaStream_t s, const CUtensorMap* X = nullptr, const CUtensorMap* Xs = nullptr) {
   constexpr int smem = gemm2_smem_bytes<STAGES, RES, XS>();
   static bool attr_done[64] = {false};
   int dev = 0;
@@ -324,8 +339,8 @@ static void launch_pair(const CUtensorMap& A, const CUtensorMap& B, int M, int N
   if (tiles < pairs) pairs = tiles;
   if (pairs <= 0) return;
   GemmShape sh{M, N, K, b_off, err};
-  launch_pdl(k_gemm2<STAGES, RES, XS, Epi>, dim3(2 * pairs), dim3(GEMM2_THREADS), smem, s, A, B, X ? *X : A, sh,
-             epi);
+  launch_pdl(k_gemm2<STAGES, RES, XS, Epi>, dim3(2 * pairs), dim3(GEMM2_THREADS), smem, s, A, B, X ? *X : A,
+             Xs ? *Xs : A, sh, epi);
 }
 
 template <class Epi>
@@ -373,12 +388,13 @@ void gemm_pair_gelu(const CUtensorMap& A, const CUtensorMap& B, int M, int b_off
   launch_pair<6, false, 0>(A, B, M, FF, DIM, b_off, e, err, s);
 }
 
-void gemm_pair_gate_res(const CUtensorMap& A, const CUtensorMap& B, const CUtensorMap& X, int M, int K, int b_off,
-                        const float* bias, const float* gate, float* x, int* err, cudaStream_t s) {
+void gemm_pair_gate_res(const CUtensorMap& A, const CUtensorMap& B, const CUtensorMap& X, const CUtensorMap& Xs,
+                        int M, int K, int b_off, const float* bias, const float* gate, float* x, int* err,
+                        cudaStream_t s) {
   EpiGateResSmem e{bias, gate, x};
   // 5 operand stages + 2 residual slots (same shared memory as 4 + 3):
   // measured FF2 -5.7%, the out projection unchanged
-  launch_pair<5, true, 2>(A, B, M, DIM, K, b_off, e, err, s, &X);
+  launch_pair<5, true, 2>(A, B, M, DIM, K, b_off, e, err, s, &X, &Xs);
 }
 
 void gemm_pair_f32(const CUtensorMap& A, const CUtensorMap& B, int M, int N, int K, const float* bias, float* out,

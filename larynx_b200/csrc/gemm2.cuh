@@ -200,6 +200,59 @@ __device__ __forceinline__ bool epi_step2(const Epi& epi, const uint8_t* sX, uin
   return true;
 }
 
+// One 32-column residual step stored by TMA: the warp's 32 rows of the box
+// are updated in place (o = epi.apply(v, x) written over x in the same
+// swizzled positions), and lane 0 stores the warp's 32 x 32 sub-box with one
+// bulk tensor copy (rows past the tensor are not written).  The slot is
+// released once the copy has read shared memory.  Compared with each thread
+// storing its row's 128 bytes, the LSU issues nothing for the output and the
+// copy engine writes whole lines.
+template <class Epi>
+__device__ __forceinline__ bool epi_res_store_step(const Epi& epi, uint8_t* sX, uint64_t* x_full, uint64_t* x_empty,
+                                                   int& slot, uint32_t& xph, int xs, int half, int q, int rt,
+                                                   int row0, int col, const GemmShape& sh, const CUtensorMap* tmXs,
+                                                   volatile int* abort_flag, const float (&v0)[16],
+                                                   const float (&v1)[16]) {
+  constexpr int XBOX = G2_HALF * 32 * 4;
+  const bool ok = mbar_wait(&x_full[slot], xph, sh.err, abort_flag, DEV_TIMEOUT_EPILOGUE);
+  if (!__all_sync(0xffffffffu, ok)) return false;
+  uint8_t* box = sX + (2 * slot + half) * XBOX;
+  uint8_t* xrow = box + rt * 128;
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+    float xin[16], o[16];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float4 f = *reinterpret_cast<const float4*>(xrow + (((4 * c + j) ^ (rt & 7)) << 4));
+      xin[4 * j + 0] = f.x;
+      xin[4 * j + 1] = f.y;
+      xin[4 * j + 2] = f.z;
+      xin[4 * j + 3] = f.w;
+    }
+    epi.apply(col + 16 * c, c ? v1 : v0, xin, o);
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      *reinterpret_cast<float4*>(xrow + (((4 * c + j) ^ (rt & 7)) << 4)) =
+          make_float4(o[4 * j + 0], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
+  }
+  fence_proxy_async_smem();  // the generic-proxy writes, before the async-proxy read
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) {
+    const int y = row0 + 32 * q;  // first row of this warp's sub-box
+    if (y < sh.M) {
+      tma_store_2d(tmXs, box + q * 32 * 128, col, y);
+      bulk_commit_group();
+      bulk_wait_group_read0();
+    }
+    mbar_arrive(&x_empty[slot]);
+  }
+  if (++slot == xs) {
+    slot = 0;
+    xph ^= 1u;
+  }
+  return true;
+}
+
 template <int STAGES, bool RES, int XS>
 __host__ __device__ constexpr int gemm2_smem_bytes() {
   return 1024 + STAGES * 2 * (G2_HALF * G2_BK * 2) + (RES ? XS * 2 * G2_HALF * 32 * 4 : 0) + 512;
@@ -208,7 +261,8 @@ __host__ __device__ constexpr int gemm2_smem_bytes() {
 template <int STAGES, bool RES, int XS, class Epi>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM2_THREADS, 1)
     k_gemm2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-            const __grid_constant__ CUtensorMap tmX, GemmShape sh, Epi epi) {
+            const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmXs, GemmShape sh,
+            Epi epi) {
   constexpr int A_BYTES = G2_HALF * G2_BK * 2;  // 16 KB
   constexpr int B_BYTES = G2_HALF * G2_BK * 2;  // 16 KB
   constexpr int XBOX = G2_HALF * 32 * 4;        // 16 KB: 128 rows x 32 fp32 columns
@@ -255,6 +309,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM2_THREADS, 1)
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
     if (RES) tma_prefetch_desc(&tmX);
+    if (RES) tma_prefetch_desc(&tmXs);
   }
   __syncwarp();
   if (warp == 1) {
@@ -395,13 +450,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM2_THREADS, 1)
       for (int j = 0; j < G2_STEPS && ok; j += 2) {
         // TMEM load of step j + 1 in flight while step j is processed
         tmem_ld32x2(t_row + 32 * (j + 1), b0, b1);
-        ok = epi_step2<RES>(epi, sX, x_full, x_empty, slot, xph, XS_, half, rt, row, n0 + 32 * j, sh, abort_flag,
-                            a0, a1);
+        if constexpr (RES)
+          ok = epi_res_store_step(epi, sX, x_full, x_empty, slot, xph, XS_, half, q, rt, m0, n0 + 32 * j, sh, &tmXs,
+                                  abort_flag, a0, a1);
+        else
+          ok = epi_step2<RES>(epi, sX, x_full, x_empty, slot, xph, XS_, half, rt, row, n0 + 32 * j, sh, abort_flag,
+                              a0, a1);
         tmem_ld_wait();
         if (!ok) break;
         if (j + 2 < G2_STEPS) tmem_ld32x2(t_row + 32 * (j + 2), a0, a1);
-        ok = epi_step2<RES>(epi, sX, x_full, x_empty, slot, xph, XS_, half, rt, row, n0 + 32 * (j + 1), sh,
-                            abort_flag, b0, b1);
+        if constexpr (RES)
+          ok = epi_res_store_step(epi, sX, x_full, x_empty, slot, xph, XS_, half, q, rt, m0, n0 + 32 * (j + 1), sh,
+                                  &tmXs, abort_flag, b0, b1);
+        else
+          ok = epi_step2<RES>(epi, sX, x_full, x_empty, slot, xph, XS_, half, rt, row, n0 + 32 * (j + 1), sh,
+                              abort_flag, b0, b1);
         tmem_ld_wait();
       }
       if (!ok) break;
@@ -416,6 +479,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM2_THREADS, 1)
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
+    // the residual stores' global writes complete before the CTA exits
+    if (RES && lane == 0) bulk_wait_group0();
   }
 
   __syncwarp();

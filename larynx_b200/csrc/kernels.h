@@ -136,8 +136,11 @@ void gemm_pair_qkv(const CUtensorMap& A, const CUtensorMap& B, int M, int b_off,
                    bf16* k, __half* v, const int* pos, const float2* rope, int* err, cudaStream_t s);
 void gemm_pair_gelu(const CUtensorMap& A, const CUtensorMap& B, int M, int b_off, const float* bias, bf16* h,
                     int* err, cudaStream_t s);
-void gemm_pair_gate_res(const CUtensorMap& A, const CUtensorMap& B, const CUtensorMap& X, int M, int K, int b_off,
-                        const float* bias, const float* gate, float* x, int* err, cudaStream_t s);
+// X: the fp32 residual x with box 128 x 32 (loads); Xs: the same tensor with
+// box 32 x 32 (the epilogue's TMA stores of each warp's 32 rows).
+void gemm_pair_gate_res(const CUtensorMap& A, const CUtensorMap& B, const CUtensorMap& X, const CUtensorMap& Xs,
+                        int M, int K, int b_off, const float* bias, const float* gate, float* x, int* err,
+                        cudaStream_t s);
 // causal grouped conv (k=31, 16 groups) over the staged rows [0, Ms); B box 64 x 64.
 // second == 0: out_stage[srow] = bf16(mish(conv + bias))  (rows with s2p >= 0)
 // second == 1: x[s2p[srow]] += mish(conv + bias)
