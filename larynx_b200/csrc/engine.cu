@@ -465,8 +465,11 @@ int ensure_workspace(lx_flow* h, const Plan& p, size_t in_floats, int n_utt) {
                     static_cast<size_t>(n_utt) > w.capUtt;
   if (grow) {
     clear_graphs(h);
-    void** ptrs[] = {(void**)&w.x,       (void**)&w.xn,        (void**)&w.q,        (void**)&w.k,
-                     (void**)&w.v,       (void**)&w.ao,        (void**)&w.h,        (void**)&w.stage1,
+    // q, k and v are one block (k and v point into it)
+    w.k = nullptr;
+    w.v = nullptr;
+    void** ptrs[] = {(void**)&w.x,       (void**)&w.xn,        (void**)&w.q,
+                     (void**)&w.ao,        (void**)&w.h,        (void**)&w.stage1,
                      (void**)&w.stage2,  (void**)&w.cst,       (void**)&w.a_cond,   (void**)&w.xb,
                      (void**)&w.dphi,    (void**)&w.xs,        (void**)&w.pos,      (void**)&w.p2s,
                      (void**)&w.s2p,     (void**)&w.frame_utt, (void**)&w.seq_rows, (void**)&w.frame_rows,
@@ -484,8 +487,7 @@ int ensure_workspace(lx_flow* h, const Plan& p, size_t in_floats, int n_utt) {
     const size_t R = w.capR, Rs = w.capRs, F = w.capF;
     int rc;
     if ((rc = dev_alloc(h, &w.x, R * DIM, false)) || (rc = dev_alloc(h, &w.xn, R * DIM, false)) ||
-        (rc = dev_alloc(h, &w.q, R * DIM, false)) || (rc = dev_alloc(h, &w.k, R * DIM, false)) ||
-        (rc = dev_alloc(h, &w.v, R * DIM, false)) ||
+        (rc = dev_alloc(h, &w.q, 3 * R * DIM, false)) ||
         (rc = dev_alloc(h, &w.ao, R * DIM, false)) || (rc = dev_alloc(h, &w.h, R * FF, false)) ||
         (rc = dev_alloc(h, &w.stage1, Rs * DIM, false)) || (rc = dev_alloc(h, &w.stage2, Rs * DIM, false)) ||
         (rc = dev_alloc(h, &w.cst, R * DIM, false)) || (rc = dev_alloc(h, &w.a_cond, R * COND_K, false)) ||
@@ -499,13 +501,13 @@ int ensure_workspace(lx_flow* h, const Plan& p, size_t in_floats, int n_utt) {
         (rc = dev_alloc(h, &w.in_noise, w.capIn, false)) || (rc = dev_alloc(h, &w.out_mel, w.capIn, false)) ||
         (rc = dev_alloc(h, &w.in_spks, w.capUtt * MEL, false)))
       return rc;
+    w.k = w.q + R * DIM;
+    w.v = reinterpret_cast<__half*>(w.q + 2 * R * DIM);
     // every buffer starts finite: rows that no kernel writes (alignment gaps,
     // rows past the last sequence, staging gap rows) are read as operands
     CK(cudaMemset(w.x, 0, R * DIM * 4));
     CK(cudaMemset(w.xn, 0, R * DIM * 2));
-    CK(cudaMemset(w.q, 0, R * DIM * 2));
-    CK(cudaMemset(w.k, 0, R * DIM * 2));
-    CK(cudaMemset(w.v, 0, R * DIM * 2));
+    CK(cudaMemset(w.q, 0, 3 * R * DIM * 2));
     CK(cudaMemset(w.ao, 0, R * DIM * 2));
     CK(cudaMemset(w.h, 0, R * FF * 2));
     CK(cudaMemset(w.stage1, 0, Rs * DIM * 2));
@@ -515,6 +517,7 @@ int ensure_workspace(lx_flow* h, const Plan& p, size_t in_floats, int n_utt) {
     ok &= tmap_bf16(&w.tm_xn, w.xn, R, DIM, DIM, 128, 64);
     ok &= tmap_bf16(&w.tm_ao, w.ao, R, DIM, DIM, 128, 64);
     ok &= tmap_bf16(&w.tm_h, w.h, R, FF, FF, 128, 64);
+    ok &= tmap_bf16(&w.tm_hs, w.h, R, FF, FF, 32, 64);
     ok &= tmap_bf16(&w.tm_xb, w.xb, R, MEL, MEL, 128, 64);
     ok &= tmap_bf16(&w.tm_acond, w.a_cond, R, COND_K, COND_K, 128, 64);
     ok &= tmap_bf16(&w.tm_stage1, w.stage1, Rs, DIM, DIM, CONV_WIN_ROWS, 64);
@@ -522,6 +525,7 @@ int ensure_workspace(lx_flow* h, const Plan& p, size_t in_floats, int n_utt) {
     ok &= tmap_bf16(&w.tm_q, w.q, R, DIM, DIM, 128, 64);
     ok &= tmap_bf16(&w.tm_k, w.k, R, DIM, DIM, 128, 64);
     ok &= tmap_bf16(&w.tm_v, w.v, R, DIM, DIM, 128, 64);
+    ok &= tmap_bf16(&w.tm_qkvs, w.q, 3 * R, DIM, DIM, 32, 64);
     ok &= tmap_f32(&w.tm_x, w.x, R, DIM, DIM, 128, 32);
     ok &= tmap_f32(&w.tm_xs, w.x, R, DIM, DIM, 32, 32);
     if (!ok) return h->fail(LX_ERR_CUDA, "cuTensorMapEncodeTiled failed for a workspace tensor");
@@ -605,8 +609,8 @@ void enqueue_dit(lx_flow* h, const Plan& p, const float* mod, const float* mod_f
     timed(h, K_ADALN, s, [&] { adaln_rows(w.x, w.xn, m + 0 * DIM, m + 1 * DIM, R, s); });
     timed(h, K_QKV, s, [&] {
       if (pair_q)
-        gemm_pair_qkv(w.tm_xn, W.tm_wqkv[0], R, l * QKV_N, W.bqkv + static_cast<size_t>(l) * QKV_N, w.q, w.k, w.v,
-                      w.pos, W.rope, err, s);
+        gemm_pair_qkv(w.tm_xn, W.tm_wqkv[0], w.tm_qkvs, static_cast<int>(w.capR), R, l * QKV_N,
+                      W.bqkv + static_cast<size_t>(l) * QKV_N, w.q, w.k, w.v, w.pos, W.rope, err, s);
       else
         gemm_qkv(bnq, w.tm_xn, W.tm_wqkv[iq], R, l * QKV_N, W.bqkv + static_cast<size_t>(l) * QKV_N, w.q, w.k, w.v,
                  w.pos, W.rope, err, s);
@@ -624,7 +628,7 @@ void enqueue_dit(lx_flow* h, const Plan& p, const float* mod, const float* mod_f
     timed(h, K_ADALN, s, [&] { adaln_rows(w.x, w.xn, m + 3 * DIM, m + 4 * DIM, R, s); });
     timed(h, K_FF1, s, [&] {
       if (pair_f)
-        gemm_pair_gelu(w.tm_xn, W.tm_w1[0], R, l * FF, W.b1 + static_cast<size_t>(l) * FF, w.h, err, s);
+        gemm_pair_gelu(w.tm_xn, W.tm_w1[0], w.tm_hs, R, l * FF, W.b1 + static_cast<size_t>(l) * FF, w.h, err, s);
       else
         gemm_gelu(bnf, w.tm_xn, W.tm_w1[iff], R, l * FF, W.b1 + static_cast<size_t>(l) * FF, w.h, err, s);
     });
@@ -801,7 +805,8 @@ void lx_flow_destroy(lx_flow* h) {
   cudaStreamSynchronize(h->stream);
   clear_graphs(h);
   Workspace& w = h->ws;
-  void* ws_ptrs[] = {w.x,        w.xn,       w.q,          w.k,         w.v,        w.ao,       w.h,
+  // (w.k and w.v point into w.q's block)
+  void* ws_ptrs[] = {w.x,        w.xn,       w.q,          w.ao,       w.h,
                      w.stage1,   w.stage2,   w.cst,        w.a_cond,    w.xb,        w.dphi,     w.xs,
                      w.pos,      w.p2s,      w.s2p,        w.frame_utt, w.seq_rows,  w.frame_rows, w.frame_src,
                      w.tiles,    w.in_mu,    w.in_cond,    w.in_noise,  w.out_mel,   w.in_spks,  w.cap,

@@ -86,6 +86,8 @@ struct Workspace {
   CUtensorMap tm_xn, tm_ao, tm_h, tm_xb, tm_acond, tm_stage1, tm_stage2, tm_q, tm_k, tm_v;
   CUtensorMap tm_x;   // fp32 residual stream, box 128 x 32
   CUtensorMap tm_xs;  // the same, box 32 x 32 (TMA stores of the residual GEMM epilogue)
+  CUtensorMap tm_hs;  // FF hidden h, box 32 x 64 (TMA stores of the GELU GEMM epilogue)
+  CUtensorMap tm_qkvs;  // q, k, v as one [3 capR][1024] block, box 32 x 64 (QKV GEMM epilogue stores)
   uint64_t generation = 0;
 };
 

@@ -137,32 +137,52 @@ __device__ __forceinline__ void add_bias16(float (&v)[16], const float* bias) {
 }
 
 struct EpiQKV {
+  // the pair kernel stages the q / k (bf16) and v (fp16) values and stores
+  // them by TMA through one map over the three planes q, k, v (contiguous,
+  // plane_rows rows apart)
+  static constexpr bool kStageBf16 = true;
   const float* bias;
   bf16* q;
   bf16* k;
   __half* v;  // fp16 [M][1024]: the MN-major B operand of the attention PV MMA
   const int* pos;
   const float2* rope;  // [pos][32] (cos, sin)
-  __device__ __forceinline__ void operator()(int row, int col0, float (&v16)[16]) const {
+  int plane_rows;      // rows between the q, k and v planes (0 when they are not one block)
+  // bias, then the partial rotary of q and k (GPT-J pairs (2i, 2i+1) of
+  // channels 0..63, angle pos * inv_freq[i])
+  __device__ __forceinline__ void apply(int row, int col0, float (&v16)[16]) const {
     add_bias16(v16, bias + col0);
+    const int c = col0 & (DIM - 1);
+    if ((col0 >> 10) < 2 && c < HDIM) {
+      const float2* cs = rope + static_cast<size_t>(__ldg(pos + row)) * 32 + (c >> 1);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float2 t = __ldg(cs + i);
+        const float x0 = v16[2 * i], x1 = v16[2 * i + 1];
+        v16[2 * i] = x0 * t.x - x1 * t.y;
+        v16[2 * i + 1] = x1 * t.x + x0 * t.y;
+      }
+    }
+  }
+  __device__ __forceinline__ uint32_t pack2(int col0, float lo, float hi) const {
+    return (col0 >> 10) < 2 ? pack_bf16x2(lo, hi) : pack_f16x2(lo, hi);
+  }
+  __device__ __forceinline__ void* out_ptr(int row, int col0) const {
+    const int which = col0 >> 10;
+    const size_t off = static_cast<size_t>(row) * DIM + (col0 & (DIM - 1));
+    return which == 0 ? static_cast<void*>(q + off) : which == 1 ? static_cast<void*>(k + off)
+                                                                 : static_cast<void*>(v + off);
+  }
+  __device__ __forceinline__ int store_x(int col0) const { return col0 & (DIM - 1); }
+  __device__ __forceinline__ int store_y(int col0, int row) const { return (col0 >> 10) * plane_rows + row; }
+  __device__ __forceinline__ void operator()(int row, int col0, float (&v16)[16]) const {
+    apply(row, col0, v16);
     const int which = col0 >> 10;
     const int c = col0 & (DIM - 1);
-    if (which < 2) {
-      if (c < HDIM) {
-        // partial rotary, GPT-J pairs (2i, 2i+1), angle pos * inv_freq[i]
-        const float2* cs = rope + static_cast<size_t>(__ldg(pos + row)) * 32 + (c >> 1);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float2 t = __ldg(cs + i);
-          const float x0 = v16[2 * i], x1 = v16[2 * i + 1];
-          v16[2 * i] = x0 * t.x - x1 * t.y;
-          v16[2 * i + 1] = x1 * t.x + x0 * t.y;
-        }
-      }
+    if (which < 2)
       store_bf16x16((which == 0 ? q : k) + static_cast<size_t>(row) * DIM + c, v16);
-    } else {
+    else
       store_f16x16(v + static_cast<size_t>(row) * DIM + c, v16);
-    }
   }
 };
 
@@ -193,6 +213,7 @@ struct EpiGateRes {
 // x[row, col] = xin + gate[col] * (acc + bias[col]); xin is the residual tile
 // the loader warp staged in shared memory (MODE_RESID)
 struct EpiGateResSmem {
+  static constexpr bool kStageBf16 = false;
   const float* bias;
   const float* gate;
   float* x;
@@ -231,6 +252,17 @@ struct EpiGateResSmem {
 struct EpiGelu {
   const float* bias;
   bf16* h;
+  // the pair kernel stages GELU(acc + bias) as bf16 and stores it by TMA
+  static constexpr bool kStageBf16 = true;
+  __device__ __forceinline__ void* out_ptr(int row, int col0) const { return h + static_cast<size_t>(row) * FF + col0; }
+  __device__ __forceinline__ int store_x(int col0) const { return col0; }
+  __device__ __forceinline__ int store_y(int, int row) const { return row; }
+  __device__ __forceinline__ uint32_t pack2(int, float lo, float hi) const { return pack_bf16x2(lo, hi); }
+  __device__ __forceinline__ void apply(int, int col0, float (&v)[16]) const {
+    add_bias16(v, bias + col0);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = gelu_tanh_fast(v[j]);
+  }
   __device__ __forceinline__ void operator()(int row, int col0, float (&v)[16]) const {
     add_bias16(v, bias + col0);
 #pragma unroll
@@ -240,6 +272,7 @@ struct EpiGelu {
 };
 
 struct EpiF32 {
+  static constexpr bool kStageBf16 = false;
   const float* bias;
   float* out;
   int ldo;
@@ -326,7 +359,7 @@ static void launch(const CUtensorMap& A, const CUtensorMap& B, int M, int N, int
 template <int STAGES, bool RES, int XS, class Epi>
 static void launch_pair(const CUtensorMap& A, const CUtensorMap& B, int M, int N, int K, int b_off, const Epi& epi,
                         int* err, cudaStream_t s, const CUtensorMap* X = nullptr, const CUtensorMap* Xs = nullptr) {
-  constexpr int smem = gemm2_smem_bytes<STAGES, RES, XS>();
+  constexpr int smem = gemm2_smem_bytes<STAGES, RES, XS, Epi::kStageBf16>();
   static bool attr_done[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -360,7 +393,7 @@ int pick_bn(int M, int N) {
 
 void gemm_qkv(int bn, const CUtensorMap& A, const CUtensorMap& B, int M, int b_off, const float* bias, bf16* q,
               bf16* k, __half* v, const int* pos, const float2* rope, int* err, cudaStream_t s) {
-  EpiQKV e{bias, q, k, v, pos, rope};
+  EpiQKV e{bias, q, k, v, pos, rope, 0};
   launch_bn(bn, A, B, M, QKV_N, DIM, b_off, e, err, s);
 }
 
@@ -376,16 +409,17 @@ void gemm_gate_res_tma(const CUtensorMap& A, const CUtensorMap& B, const CUtenso
   launch<128, 4, MODE_RESID>(A, B, M, DIM, K, b_off, e, err, s, &X);
 }
 
-void gemm_pair_qkv(const CUtensorMap& A, const CUtensorMap& B, int M, int b_off, const float* bias, bf16* q,
-                   bf16* k, __half* v, const int* pos, const float2* rope, int* err, cudaStream_t s) {
-  EpiQKV e{bias, q, k, v, pos, rope};
-  launch_pair<6, false, 0>(A, B, M, QKV_N, DIM, b_off, e, err, s);
+void gemm_pair_qkv(const CUtensorMap& A, const CUtensorMap& B, const CUtensorMap& QKVs, int plane_rows, int M,
+                   int b_off, const float* bias, bf16* q, bf16* k, __half* v, const int* pos, const float2* rope,
+                   int* err, cudaStream_t s) {
+  EpiQKV e{bias, q, k, v, pos, rope, plane_rows};
+  launch_pair<6, false, 0>(A, B, M, QKV_N, DIM, b_off, e, err, s, nullptr, &QKVs);
 }
 
-void gemm_pair_gelu(const CUtensorMap& A, const CUtensorMap& B, int M, int b_off, const float* bias, bf16* h,
-                    int* err, cudaStream_t s) {
+void gemm_pair_gelu(const CUtensorMap& A, const CUtensorMap& B, const CUtensorMap& Hs, int M, int b_off,
+                    const float* bias, bf16* h, int* err, cudaStream_t s) {
   EpiGelu e{bias, h};
-  launch_pair<6, false, 0>(A, B, M, FF, DIM, b_off, e, err, s);
+  launch_pair<6, false, 0>(A, B, M, FF, DIM, b_off, e, err, s, nullptr, &Hs);
 }
 
 void gemm_pair_gate_res(const CUtensorMap& A, const CUtensorMap& B, const CUtensorMap& X, const CUtensorMap& Xs,

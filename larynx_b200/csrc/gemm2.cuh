@@ -200,6 +200,15 @@ __device__ __forceinline__ bool epi_step2(const Epi& epi, const uint8_t* sX, uin
   return true;
 }
 
+// A box whose 32 rows reach past the last row is not stored by TMA (its
+// tensor map spans the workspace's capacity, beyond M): each lane copies its
+// own row, if it is a valid one, from the swizzled box to global memory.
+__device__ __forceinline__ void copy_staged_row(const uint8_t* srow, int r, void* dst) {
+#pragma unroll
+  for (int u = 0; u < 8; ++u)
+    reinterpret_cast<uint4*>(dst)[u] = *reinterpret_cast<const uint4*>(srow + ((u ^ (r & 7)) << 4));
+}
+
 // One 32-column residual step stored by TMA: the warp's 32 rows of the box
 // are updated in place (o = epi.apply(v, x) written over x in the same
 // swizzled positions), and lane 0 stores the warp's 32 x 32 sub-box with one
@@ -237,15 +246,18 @@ __device__ __forceinline__ bool epi_res_store_step(const Epi& epi, uint8_t* sX, 
   }
   fence_proxy_async_smem();  // the generic-proxy writes, before the async-proxy read
   __syncwarp();
-  if ((threadIdx.x & 31) == 0) {
-    const int y = row0 + 32 * q;  // first row of this warp's sub-box
-    if (y < sh.M) {
+  const int y = row0 + 32 * q;  // first row of this warp's sub-box
+  if (y + 32 <= sh.M) {
+    if ((threadIdx.x & 31) == 0) {
       tma_store_2d(tmXs, box + q * 32 * 128, col, y);
       bulk_commit_group();
       bulk_wait_group_read0();
     }
-    mbar_arrive(&x_empty[slot]);
+  } else if (y + (rt & 31) < sh.M) {
+    copy_staged_row(xrow, rt, epi.x + static_cast<size_t>(y + (rt & 31)) * DIM + col);
   }
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(&x_empty[slot]);
   if (++slot == xs) {
     slot = 0;
     xph ^= 1u;
@@ -253,9 +265,32 @@ __device__ __forceinline__ bool epi_res_store_step(const Epi& epi, uint8_t* sX, 
   return true;
 }
 
-template <int STAGES, bool RES, int XS>
+// Half of a staged 64-column box: 32 columns of this thread's row (v0, v1)
+// through epi.apply, packed to bf16 and written as 16-byte units u0 .. u0 + 3
+// of the row in the 128-byte swizzle the box's TMA store reads.
+template <class Epi>
+__device__ __forceinline__ void stage_bf16_half(const Epi& epi, uint8_t* stg, int r, int grow, int col,
+                                                float (&v0)[16], float (&v1)[16], int u0) {
+  epi.apply(grow, col, v0);
+  epi.apply(grow, col + 16, v1);
+  uint8_t* row = stg + r * 128;
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const float* a = u < 2 ? v0 + 8 * u : v1 + 8 * (u - 2);
+    *reinterpret_cast<uint4*>(row + (((u0 + u) ^ (r & 7)) << 4)) =
+        make_uint4(epi.pack2(col, a[0], a[1]), epi.pack2(col, a[2], a[3]), epi.pack2(col, a[4], a[5]),
+                   epi.pack2(col, a[6], a[7]));
+  }
+}
+
+// Staged bf16 epilogue (Epi::kStageBf16): each epilogue warp owns a 32-row x
+// 64-column bf16 box (4 KB, 128-byte swizzle) in shared memory.
+constexpr int G2_STAGE_BYTES = 32 * 128;
+
+template <int STAGES, bool RES, int XS, bool STG = false>
 __host__ __device__ constexpr int gemm2_smem_bytes() {
-  return 1024 + STAGES * 2 * (G2_HALF * G2_BK * 2) + (RES ? XS * 2 * G2_HALF * 32 * 4 : 0) + 512;
+  return 1024 + STAGES * 2 * (G2_HALF * G2_BK * 2) + (RES ? XS * 2 * G2_HALF * 32 * 4 : 0) +
+         (STG ? 8 * G2_STAGE_BYTES : 0) + 512;
 }
 
 template <int STAGES, bool RES, int XS, class Epi>
@@ -270,13 +305,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM2_THREADS, 1)
   constexpr uint32_t TMEM_COLS = 2 * G2_BN;     // two accumulator stages
   constexpr uint32_t IDESC = idesc_bf16_f32(G2_BM, G2_BN);
   constexpr int XS_ = RES ? XS : 1;
+  constexpr bool STG = Epi::kStageBf16;
+  static_assert(!(STG && RES), "the staged bf16 epilogue has no residual");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
   uint8_t* sX = sB + STAGES * B_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sX + (RES ? XS * XSLOT : 0));
+  uint8_t* sStg = sX + (RES ? XS * XSLOT : 0);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sStg + (STG ? 8 * G2_STAGE_BYTES : 0));
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -309,7 +347,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM2_THREADS, 1)
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
     if (RES) tma_prefetch_desc(&tmX);
-    if (RES) tma_prefetch_desc(&tmXs);
+    if (RES || STG) tma_prefetch_desc(&tmXs);
   }
   __syncwarp();
   if (warp == 1) {
@@ -446,8 +484,34 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM2_THREADS, 1)
       float a0[16], a1[16], b0[16], b1[16];
       tmem_ld32x2(t_row, a0, a1);
       tmem_ld_wait();
+      if constexpr (STG) {
+        // two 32-column steps fill the warp's 32 x 64 box; one TMA store each
+        uint8_t* stg = sStg + (warp - G2_EPI_WARP0) * G2_STAGE_BYTES;
+        const int y = m0 + 32 * q;
 #pragma unroll 1
-      for (int j = 0; j < G2_STEPS && ok; j += 2) {
+        for (int j = 0; j < G2_STEPS; j += 2) {
+          tmem_ld32x2(t_row + 32 * (j + 1), b0, b1);
+          if (lane == 0) bulk_wait_group_read0();  // the previous box has been read
+          __syncwarp();
+          stage_bf16_half(epi, stg, lane, y + lane, n0 + 32 * j, a0, a1, 0);
+          tmem_ld_wait();
+          if (j + 2 < G2_STEPS) tmem_ld32x2(t_row + 32 * (j + 2), a0, a1);
+          stage_bf16_half(epi, stg, lane, y + lane, n0 + 32 * (j + 1), b0, b1, 4);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (y + 32 <= sh.M) {
+            if (lane == 0) {
+              tma_store_2d(&tmXs, stg, epi.store_x(n0 + 32 * j), epi.store_y(n0 + 32 * j, y));
+              bulk_commit_group();
+            }
+          } else if (y + lane < sh.M) {
+            copy_staged_row(stg + lane * 128, lane, epi.out_ptr(y + lane, n0 + 32 * j));
+          }
+          tmem_ld_wait();
+        }
+      }
+#pragma unroll 1
+      for (int j = 0; !STG && j < G2_STEPS && ok; j += 2) {
         // TMEM load of step j + 1 in flight while step j is processed
         tmem_ld32x2(t_row + 32 * (j + 1), b0, b1);
         if constexpr (RES)
@@ -479,8 +543,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM2_THREADS, 1)
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
-    // the residual stores' global writes complete before the CTA exits
-    if (RES && lane == 0) bulk_wait_group0();
+    // the TMA stores' global writes complete before the CTA exits
+    if ((RES || STG) && lane == 0) bulk_wait_group0();
   }
 
   __syncwarp();

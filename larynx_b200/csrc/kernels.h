@@ -132,10 +132,15 @@ void gemm_in_proj(int bn, const CUtensorMap& A, const CUtensorMap& B, int M, con
 bool use_pair_gemm(int M, int N);
 void gemm_pair_f32(const CUtensorMap& A, const CUtensorMap& B, int M, int N, int K, const float* bias, float* out,
                    int ldo, int* err, cudaStream_t s);
-void gemm_pair_qkv(const CUtensorMap& A, const CUtensorMap& B, int M, int b_off, const float* bias, bf16* q,
-                   bf16* k, __half* v, const int* pos, const float2* rope, int* err, cudaStream_t s);
-void gemm_pair_gelu(const CUtensorMap& A, const CUtensorMap& B, int M, int b_off, const float* bias, bf16* h,
-                    int* err, cudaStream_t s);
+// QKVs: q, k and v as one [3 x plane_rows][1024] block (k = q + plane_rows
+// rows, v = q + 2 plane_rows rows; v's fp16 bits moved as 16-bit elements)
+// with box 32 rows x 64 columns (the epilogue's TMA stores).
+void gemm_pair_qkv(const CUtensorMap& A, const CUtensorMap& B, const CUtensorMap& QKVs, int plane_rows, int M,
+                   int b_off, const float* bias, bf16* q, bf16* k, __half* v, const int* pos, const float2* rope,
+                   int* err, cudaStream_t s);
+// Hs: h with box 32 rows x 64 columns (the epilogue's TMA stores).
+void gemm_pair_gelu(const CUtensorMap& A, const CUtensorMap& B, const CUtensorMap& Hs, int M, int b_off,
+                    const float* bias, bf16* h, int* err, cudaStream_t s);
 // X: the fp32 residual x with box 128 x 32 (loads); Xs: the same tensor with
 // box 32 x 32 (the epilogue's TMA stores of each warp's 32 rows).
 void gemm_pair_gate_res(const CUtensorMap& A, const CUtensorMap& B, const CUtensorMap& X, const CUtensorMap& Xs,
