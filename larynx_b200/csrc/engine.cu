@@ -513,6 +513,7 @@ int ensure_workspace(lx_flow* h, const Plan& p, size_t in_floats, int n_utt) {
     CK(cudaMemset(w.stage1, 0, Rs * DIM * 2));
     CK(cudaMemset(w.stage2, 0, Rs * DIM * 2));
     CK(cudaMemset(w.xb, 0, R * MEL * 2));
+    CK(cudaMemset(w.pos, 0, R * sizeof(int)));
     bool ok = true;
     ok &= tmap_bf16(&w.tm_xn, w.xn, R, DIM, DIM, 128, 64);
     ok &= tmap_bf16(&w.tm_ao, w.ao, R, DIM, DIM, 128, 64);

@@ -268,11 +268,16 @@ __device__ __forceinline__ bool epi_res_store_step(const Epi& epi, uint8_t* sX, 
 // Half of a staged 64-column box: 32 columns of this thread's row (v0, v1)
 // through epi.apply, packed to bf16 and written as 16-byte units u0 .. u0 + 3
 // of the row in the 128-byte swizzle the box's TMA store reads.
+// Rows at or past the last row (grow >= M) are never stored and are not
+// passed through epi.apply, which may index per-row tables (the rotary
+// position of a QKV row) that hold nothing valid there.
 template <class Epi>
-__device__ __forceinline__ void stage_bf16_half(const Epi& epi, uint8_t* stg, int r, int grow, int col,
+__device__ __forceinline__ void stage_bf16_half(const Epi& epi, uint8_t* stg, int r, int grow, int M, int col,
                                                 float (&v0)[16], float (&v1)[16], int u0) {
-  epi.apply(grow, col, v0);
-  epi.apply(grow, col + 16, v1);
+  if (grow < M) {
+    epi.apply(grow, col, v0);
+    epi.apply(grow, col + 16, v1);
+  }
   uint8_t* row = stg + r * 128;
 #pragma unroll
   for (int u = 0; u < 4; ++u) {
@@ -493,10 +498,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM2_THREADS, 1)
           tmem_ld32x2(t_row + 32 * (j + 1), b0, b1);
           if (lane == 0) bulk_wait_group_read0();  // the previous box has been read
           __syncwarp();
-          stage_bf16_half(epi, stg, lane, y + lane, n0 + 32 * j, a0, a1, 0);
+          stage_bf16_half(epi, stg, lane, y + lane, sh.M, n0 + 32 * j, a0, a1, 0);
           tmem_ld_wait();
           if (j + 2 < G2_STEPS) tmem_ld32x2(t_row + 32 * (j + 2), a0, a1);
-          stage_bf16_half(epi, stg, lane, y + lane, n0 + 32 * (j + 1), b0, b1, 4);
+          stage_bf16_half(epi, stg, lane, y + lane, sh.M, n0 + 32 * (j + 1), b0, b1, 4);
           fence_proxy_async_smem();
           __syncwarp();
           if (y + 32 <= sh.M) {
