@@ -7,12 +7,14 @@
 //               (128-byte swizzle) into a STAGES-deep shared-memory ring
 //   warp 1      TMEM allocator; lane 0 issues tcgen05.mma (M=128, N=BN, K=16)
 //               and tcgen05.commit to release ring slots / publish tiles
-//   warps 2..5  epilogue: tcgen05.ld of a 32-row TMEM lane quarter each,
-//               fused element-wise epilogue, direct global stores
+//   warps 2..9  epilogue: tcgen05.ld of a 32-row TMEM lane quarter each (two
+//               warps per quarter, one per column half of the tile), fused
+//               element-wise epilogue, direct global stores
 // The fp32 accumulator is double-buffered in tensor memory (2 x BN columns),
 // so the epilogue of tile i overlaps the MMAs of tile i+1.
 //
-// MODE_RESID adds a seventh warp that TMA-prefetches the fp32 residual tile
+// MODE_RESID has four epilogue warps (2..5) and a seventh warp that
+// TMA-prefetches the fp32 residual tile
 // (128 x BN, as 32-column 128B-swizzled boxes) into shared memory while the
 // tile's MMAs run; the epilogue reads it from there instead of waiting on HBM.
 //
