@@ -25,7 +25,10 @@
 //   warps 4..11 epilogue: warp w reads TMEM lane quarter w % 4 and column
 //               half (w - 4) / 4 (two warps per SM sub-partition hide each
 //               other's TMEM / global latencies); each warp arrives on the
-//               leader's `tempty` barrier (8 local + 8 remote arrivals)
+//               leader's `tempty` barrier (8 local + 8 remote arrivals).
+//               RES and Epi::kStageBf16 epilogues write their 32-row output
+//               boxes in shared memory and store them with TMA copies; the
+//               others store from registers.
 // Every TMA copy in this file lands in the issuing CTA's own shared memory.
 #pragma once
 
