@@ -38,7 +38,7 @@ bool pdl_enabled();
 void pdl_set_auto(bool on);
 // Batch plans of at most this many packed rows launch with PDL by default
 // (latency-bound: the single 20 s utterance is 2 x 1000 rows).
-constexpr int PDL_AUTO_MAX_ROWS = 16384;
+constexpr int PDL_AUTO_MAX_ROWS = 4096;
 // Rows per block of the warp-per-row kernels: LX_FLOW_ROWS_PER_BLOCK when set,
 // else `dflt` (the decode uses 8; the standalone ops 0); 0 = as many as
 // spread the rows over every SM in one wave, at most 16.
