@@ -10,9 +10,9 @@ every launch, lx_flow_profile_decode):
     c(T) = T * LINEAR_MS_PER_FRAME + ceil(T / 128) * 128 * T * ATTN_MS_PER_PAIR
 
 The linear term is everything whose work grows with the frame count (the
-projection GEMMs, conv-pos, AdaLN, the Euler update: 382 ms for the 47,726
+projection GEMMs, conv-pos, AdaLN, the Euler update: 369.0 ms for the 47,726
 frames of the config-3 set); the quadratic term is attention, whose work is
-its 128-row query tiles times the keys they see (200.8 ms for 49.3 M
+its 128-row query tiles times the keys they see (203.2 ms for 49.3 M
 tile-row x key pairs).  Attention runs at a lower fraction of the tensor
 peak than the GEMMs, so a FLOP count (378 MFLOP per frame + 90 kFLOP per
 frame pair) under-weights long utterances.
@@ -32,8 +32,8 @@ from typing import List, Sequence
 
 import numpy as np
 
-LINEAR_MS_PER_FRAME = 8.006e-3
-ATTN_MS_PER_PAIR = 4.071e-6
+LINEAR_MS_PER_FRAME = 7.732e-3
+ATTN_MS_PER_PAIR = 4.119e-6
 ATT_Q_TILE = 128
 
 
