@@ -332,6 +332,21 @@ __device__ __forceinline__ float gelu_tanh_fast(float x) {
   return 0.5f * x * (1.0f + t);
 }
 
+// The same GELU on a pair with packed fp32 arithmetic (fma / mul .f32x2):
+// u = x (c1 + c1 c0 x^2), GELU = 0.5 x + 0.5 x tanh(u); five packed
+// instructions and two MUFU tanh per pair instead of about twelve scalar ones.
+__device__ __forceinline__ float2 gelu_tanh_fast2(float2 x) {
+  const float c1 = 0.7978845608028654f;
+  const float k1 = 0.7978845608028654f * 0.044715f;
+  const float2 x2 = __fmul2_rn(x, x);
+  const float2 u = __fmul2_rn(__ffma2_rn(x2, make_float2(k1, k1), make_float2(c1, c1)), x);
+  float2 t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t.x) : "f"(u.x));
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t.y) : "f"(u.y));
+  const float2 hx = __fmul2_rn(x, make_float2(0.5f, 0.5f));
+  return __ffma2_rn(hx, t, hx);
+}
+
 // Mish = x * tanh(softplus(x)); softplus with torch's threshold 20.
 // Mish x * tanh(softplus(x)) through the identity
 //   tanh(log(1 + n)) = (n^2 + 2n) / (n^2 + 2n + 2),  n = e^x,

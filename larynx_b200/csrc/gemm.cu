@@ -261,12 +261,20 @@ struct EpiGelu {
   __device__ __forceinline__ void apply(int, int col0, float (&v)[16]) const {
     add_bias16(v, bias + col0);
 #pragma unroll
-    for (int j = 0; j < 16; ++j) v[j] = gelu_tanh_fast(v[j]);
+    for (int j = 0; j < 16; j += 2) {
+      const float2 g = gelu_tanh_fast2(make_float2(v[j], v[j + 1]));
+      v[j] = g.x;
+      v[j + 1] = g.y;
+    }
   }
   __device__ __forceinline__ void operator()(int row, int col0, float (&v)[16]) const {
     add_bias16(v, bias + col0);
 #pragma unroll
-    for (int j = 0; j < 16; ++j) v[j] = gelu_tanh_fast(v[j]);
+    for (int j = 0; j < 16; j += 2) {
+      const float2 g = gelu_tanh_fast2(make_float2(v[j], v[j + 1]));
+      v[j] = g.x;
+      v[j + 1] = g.y;
+    }
     store_bf16x16(h + static_cast<size_t>(row) * FF + col0, v);
   }
 };
