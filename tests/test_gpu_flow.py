@@ -249,3 +249,38 @@ def test_noise_bank_production_path(dec, tmp_path):
         assert fresh.last_error
     assert fresh.load_noise(path), fresh.last_error
     fresh.close()
+
+
+def test_decode_after_workspace_growth_matches_fresh_handle(dec, gguf_path):
+    """A handle whose workspace grew (a small batch, then one that needs more
+    rows: every buffer and tensor map is reallocated) decodes the larger
+    batch bit for bit as a fresh handle does.  The rows past the last packed
+    row of each plan are never read as valid data (the sequence of the
+    multi-GPU bench: shards, then the 20 s utterance, then the whole set)."""
+    from larynx_b200 import FlowDecoder
+    rng = np.random.default_rng(11)
+
+    def batch(lengths):
+        mus = [rng.standard_normal((80, n)).astype(np.float32) for n in lengths]
+        conds = [np.where(np.arange(n) < n // 5, rng.standard_normal((80, n)), 0).astype(np.float32)
+                 for n in lengths]
+        noise = [rng.standard_normal((80, n)).astype(np.float32) for n in lengths]
+        spks = rng.standard_normal((len(lengths), 80)).astype(np.float32)
+        return mus, conds, spks, noise
+
+    small = [131, 77, 250]
+    large = [1000, 333, 1499, 517, 64, 1201, 250, 903]  # > 4096 and > 9.5k packed rows: pair GEMMs
+    s_args = batch(small)
+    l_args = batch(large)
+    fresh = FlowDecoder(0)
+    assert fresh.load(gguf_path), fresh.last_error
+    want = fresh.decode(large, *l_args[:3], noise=l_args[3])
+    fresh.close()
+    d = FlowDecoder(0)
+    assert d.load(gguf_path), d.last_error
+    d.decode(small, *s_args[:3], noise=s_args[3])
+    d.decode([1000], *batch([1000])[:3], noise=batch([1000])[3])
+    got = d.decode(large, *l_args[:3], noise=l_args[3])
+    d.close()
+    assert np.isfinite(got).all()
+    assert np.array_equal(got, want)
