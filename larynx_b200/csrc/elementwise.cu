@@ -2,6 +2,8 @@
 // LayerNorm, the CFG Euler update, layout gathers/scatters, the load-time
 // time-embedding / modulation GEMVs, the once-per-utterance frontend, and the
 // standalone fused ops timed by the microbench.
+#include <cstdlib>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -57,16 +59,19 @@ __device__ __forceinline__ void store4(bf16* p, float4 v) {
 // variance: var = E[(x-K)^2] - E[x-K]^2, whose cancellation is bounded by
 // (mean - K)^2 / var, small for a K drawn from the row), which saves one
 // warp reduction on the latency chain of a launch that moves ~12 MB.
-template <typename Tin, typename Tout, bool PF = false>
+// REV visits the rows from the last one down (blocks are scheduled in index
+// order, so the first blocks take the rows the previous kernel wrote last).
+template <typename Tin, typename Tout, bool PF = false, bool REV = false>
 __global__ void __launch_bounds__(512) k_adaln(const Tin* __restrict__ x, Tout* __restrict__ y,
                                                 const float* __restrict__ shift, const float* __restrict__ scale,
                                                 int R) {
-  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int r0 = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int row = REV ? R - 1 - r0 : r0;
   const int lane = threadIdx.x & 31;
-  if (PF && row < R && lane == 0) prefetch_l2_bulk(x + static_cast<size_t>(row) * DIM, DIM * sizeof(Tin));
+  if (PF && r0 < R && lane == 0) prefetch_l2_bulk(x + static_cast<size_t>(row) * DIM, DIM * sizeof(Tin));
   pdl_wait();
   pdl_launch_dependents();  // after the wait: at most one dependent launch ahead
-  if (row >= R) return;
+  if (r0 >= R) return;  // r0 < R  <=>  0 <= row < R in either direction
   const Tin* xr = x + static_cast<size_t>(row) * DIM;
   float4 v[8];
 #pragma unroll
@@ -459,8 +464,21 @@ inline unsigned blocks_for(size_t n, unsigned t) { return static_cast<unsigned>(
 
 }  // namespace
 
-void adaln_rows(const float* x, bf16* y, const float* shift, const float* scale, int R, cudaStream_t s) {
-  if (R > 0) launch_pdl(k_adaln<float, bf16>, dim3((R + rows_per_block(R) - 1) / rows_per_block(R)), dim3(32 * rows_per_block(R)), 0, s, x, y, shift, scale, R);
+void adaln_rows(const float* x, bf16* y, const float* shift, const float* scale, int R, cudaStream_t s, bool rev) {
+  if (R <= 0) return;
+  const dim3 grid((R + rows_per_block(R) - 1) / rows_per_block(R)), block(32 * rows_per_block(R));
+  if (rev)
+    launch_pdl(k_adaln<float, bf16, false, true>, grid, block, 0, s, x, y, shift, scale, R);
+  else
+    launch_pdl(k_adaln<float, bf16>, grid, block, 0, s, x, y, shift, scale, R);
+}
+
+bool row_order_alternates() {
+  static const bool on = [] {
+    const char* e = getenv("LX_FLOW_ROW_ORDER");
+    return !(e && e[0] == '0');
+  }();
+  return on;
 }
 void euler_update(float* xs, const float* dphi, const int2* frame_rows, bf16* xb, int F, float dt, float cfg,
                   cudaStream_t s) {

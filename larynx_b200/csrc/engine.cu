@@ -595,6 +595,10 @@ void enqueue_dit(lx_flow* h, const Plan& p, const float* mod, const float* mod_f
   const int bn1024 = pick_bn(R, DIM), bnq = pick_bn(R, QKV_N), bnf = pick_bn(R, FF);
   const int i1024 = bn1024 == 256, iq = bnq == 256, iff = bnf == 256;
   const bool pair_q = use_pair_gemm(R, QKV_N), pair_f = use_pair_gemm(R, FF), pair_d = use_pair_gemm(R, DIM);
+  // Row direction per kernel: each row-streaming kernel starts on the rows its
+  // producer wrote last (still in L2).  out (up) -> AdaLN (down) -> FF1 (up)
+  // -> FF2 (down) -> AdaLN (up) -> QKV (down); attention reads by work item.
+  const bool alt = row_order_alternates();
   int* err = h->d_err;
   timed(h, K_INPROJ, s, [&] { gemm_in_proj(bn1024, w.tm_xb, W.tm_winx[i1024], R, w.cst, w.x, w.stage1, w.p2s, err, s); });
   timed(h, K_CONV, s, [&] { conv_pos(w.tm_stage1, W.tm_wconv[0], p.Rs, W.bconv[0], 0, w.stage2, w.x, w.s2p, err, s); });
@@ -611,7 +615,7 @@ void enqueue_dit(lx_flow* h, const Plan& p, const float* mod, const float* mod_f
     timed(h, K_QKV, s, [&] {
       if (pair_q)
         gemm_pair_qkv(w.tm_xn, W.tm_wqkv[0], w.tm_qkvs, static_cast<int>(w.capR), R, l * QKV_N,
-                      W.bqkv + static_cast<size_t>(l) * QKV_N, w.q, w.k, w.v, w.pos, W.rope, err, s);
+                      W.bqkv + static_cast<size_t>(l) * QKV_N, w.q, w.k, w.v, w.pos, W.rope, err, s, alt);
       else
         gemm_qkv(bnq, w.tm_xn, W.tm_wqkv[iq], R, l * QKV_N, W.bqkv + static_cast<size_t>(l) * QKV_N, w.q, w.k, w.v,
                  w.pos, W.rope, err, s);
@@ -626,7 +630,7 @@ void enqueue_dit(lx_flow* h, const Plan& p, const float* mod, const float* mod_f
         gemm_gate_res_tma(w.tm_ao, W.tm_wo[0], w.tm_x, R, DIM, l * DIM, W.bo + static_cast<size_t>(l) * DIM,
                           m + 2 * DIM, w.x, err, s);
     });
-    timed(h, K_ADALN, s, [&] { adaln_rows(w.x, w.xn, m + 3 * DIM, m + 4 * DIM, R, s); });
+    timed(h, K_ADALN, s, [&] { adaln_rows(w.x, w.xn, m + 3 * DIM, m + 4 * DIM, R, s, alt); });
     timed(h, K_FF1, s, [&] {
       if (pair_f)
         gemm_pair_gelu(w.tm_xn, W.tm_w1[0], w.tm_hs, R, l * FF, W.b1 + static_cast<size_t>(l) * FF, w.h, err, s);
@@ -636,7 +640,7 @@ void enqueue_dit(lx_flow* h, const Plan& p, const float* mod, const float* mod_f
     timed(h, K_FF2, s, [&] {
       if (pair_d)
         gemm_pair_gate_res(w.tm_h, W.tm_w2[0], w.tm_x, w.tm_xs, R, FF, l * DIM, W.b2 + static_cast<size_t>(l) * DIM,
-                           m + 5 * DIM, w.x, err, s);
+                           m + 5 * DIM, w.x, err, s, alt);
       else
         gemm_gate_res_tma(w.tm_h, W.tm_w2[0], w.tm_x, R, FF, l * DIM, W.b2 + static_cast<size_t>(l) * DIM,
                           m + 5 * DIM, w.x, err, s);

@@ -366,7 +366,8 @@ static void launch(const CUtensorMap& A, const CUtensorMap& B, int M, int N, int
 // CTA-pair launch: persistent grid of up to num_sms() / 2 clusters of 2.
 template <int STAGES, bool RES, int XS, class Epi>
 static void launch_pair(const CUtensorMap& A, const CUtensorMap& B, int M, int N, int K, int b_off, const Epi& epi,
-                        int* err, cudaStream_t s, const CUtensorMap* X = nullptr, const CUtensorMap* Xs = nullptr) {
+                        int* err, cudaStream_t s, const CUtensorMap* X = nullptr, const CUtensorMap* Xs = nullptr,
+                        bool rev = false) {
   constexpr int smem = gemm2_smem_bytes<STAGES, RES, XS, Epi::kStageBf16>();
   static bool attr_done[64] = {false};
   int dev = 0;
@@ -379,7 +380,7 @@ static void launch_pair(const CUtensorMap& A, const CUtensorMap& B, int M, int N
   int pairs = num_sms() / 2;
   if (tiles < pairs) pairs = tiles;
   if (pairs <= 0) return;
-  GemmShape sh{M, N, K, b_off, err};
+  GemmShape sh{M, N, K, b_off, err, rev ? 1 : 0};
   launch_pdl(k_gemm2<STAGES, RES, XS, Epi>, dim3(2 * pairs), dim3(GEMM2_THREADS), smem, s, A, B, X ? *X : A,
              Xs ? *Xs : A, sh, epi);
 }
@@ -419,24 +420,24 @@ void gemm_gate_res_tma(const CUtensorMap& A, const CUtensorMap& B, const CUtenso
 
 void gemm_pair_qkv(const CUtensorMap& A, const CUtensorMap& B, const CUtensorMap& QKVs, int plane_rows, int M,
                    int b_off, const float* bias, bf16* q, bf16* k, __half* v, const int* pos, const float2* rope,
-                   int* err, cudaStream_t s) {
+                   int* err, cudaStream_t s, bool rev) {
   EpiQKV e{bias, q, k, v, pos, rope, plane_rows};
-  launch_pair<6, false, 0>(A, B, M, QKV_N, DIM, b_off, e, err, s, nullptr, &QKVs);
+  launch_pair<6, false, 0>(A, B, M, QKV_N, DIM, b_off, e, err, s, nullptr, &QKVs, rev);
 }
 
 void gemm_pair_gelu(const CUtensorMap& A, const CUtensorMap& B, const CUtensorMap& Hs, int M, int b_off,
-                    const float* bias, bf16* h, int* err, cudaStream_t s) {
+                    const float* bias, bf16* h, int* err, cudaStream_t s, bool rev) {
   EpiGelu e{bias, h};
-  launch_pair<6, false, 0>(A, B, M, FF, DIM, b_off, e, err, s, nullptr, &Hs);
+  launch_pair<6, false, 0>(A, B, M, FF, DIM, b_off, e, err, s, nullptr, &Hs, rev);
 }
 
 void gemm_pair_gate_res(const CUtensorMap& A, const CUtensorMap& B, const CUtensorMap& X, const CUtensorMap& Xs,
                         int M, int K, int b_off, const float* bias, const float* gate, float* x, int* err,
-                        cudaStream_t s) {
+                        cudaStream_t s, bool rev) {
   EpiGateResSmem e{bias, gate, x};
   // 5 operand stages + 2 residual slots (same shared memory as 4 + 3):
   // measured FF2 -5.7%, the out projection unchanged
-  launch_pair<5, true, 2>(A, B, M, DIM, K, b_off, e, err, s, &X, &Xs);
+  launch_pair<5, true, 2>(A, B, M, DIM, K, b_off, e, err, s, &X, &Xs, rev);
 }
 
 void gemm_pair_f32(const CUtensorMap& A, const CUtensorMap& B, int M, int N, int K, const float* bias, float* out,

@@ -37,6 +37,7 @@ struct GemmShape {
   int M, N, K;
   int b_off;  // row offset into the B tensor (layer slice of stacked weights)
   int* err;   // device error word
+  int rev;    // pair GEMM: nonzero visits the 256-row blocks from the last one down
 };
 
 __host__ __device__ constexpr int tmem_cols_for(int bn) {

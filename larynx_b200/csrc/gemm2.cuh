@@ -291,6 +291,15 @@ __device__ __forceinline__ void stage_bf16_half(const Epi& epi, uint8_t* stg, in
   }
 }
 
+// 256-row block of work item `tile` (column tiles fastest).  With `rev` the
+// blocks are visited from the last one down: the rows a kernel writes last
+// are still in L2 when the next kernel starts, so the engine alternates the
+// direction from kernel to kernel and the consumer reads those rows first.
+__device__ __forceinline__ int g2_mblock(int tile, int tiles_n, int tiles_m, int rev) {
+  const int mb = tile / tiles_n;
+  return rev ? tiles_m - 1 - mb : mb;
+}
+
 // Staged bf16 epilogue (Epi::kStageBf16): each epilogue warp owns a 32-row x
 // 64-column bf16 box (4 KB, 128-byte swizzle) in shared memory.
 constexpr int G2_STAGE_BYTES = 32 * 128;
@@ -382,7 +391,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM2_THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       for (int tile = pair; tile < n_tiles; tile += n_pairs) {
-        const int m0 = (tile / tiles_n) * G2_BM + static_cast<int>(rank) * G2_HALF;
+        const int m0 = g2_mblock(tile, tiles_n, tiles_m, sh.rev) * G2_BM + static_cast<int>(rank) * G2_HALF;
         const int n0 = (tile % tiles_n) * G2_BN + static_cast<int>(rank) * G2_HALF;
         bool ok = true;
         for (int kb = 0; kb < num_kb; ++kb) {
@@ -450,7 +459,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM2_THREADS, 1)
       int slot = 0;
       uint32_t xph = 0;
       for (int tile = pair; tile < n_tiles; tile += n_pairs) {
-        const int m0 = (tile / tiles_n) * G2_BM + static_cast<int>(rank) * G2_HALF;
+        const int m0 = g2_mblock(tile, tiles_n, tiles_m, sh.rev) * G2_BM + static_cast<int>(rank) * G2_HALF;
         const int n0 = (tile % tiles_n) * G2_BN;
         bool ok = true;
         for (int j = 0; j < G2_STEPS; ++j) {
@@ -480,7 +489,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(GEMM2_THREADS, 1)
     int slot = 0;
     uint32_t xph = 0;
     for (int tile = pair; tile < n_tiles; tile += n_pairs) {
-      const int m0 = (tile / tiles_n) * G2_BM + static_cast<int>(rank) * G2_HALF;
+      const int m0 = g2_mblock(tile, tiles_n, tiles_m, sh.rev) * G2_BM + static_cast<int>(rank) * G2_HALF;
       const int n0 = (tile % tiles_n) * G2_BN + cb;
       bool ok = mbar_wait(&tfull[acc], acc_phase, sh.err, abort_flag, DEV_TIMEOUT_EPILOGUE);
       if (!__all_sync(0xffffffffu, ok)) break;

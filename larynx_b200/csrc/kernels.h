@@ -132,20 +132,22 @@ void gemm_in_proj(int bn, const CUtensorMap& A, const CUtensorMap& B, int M, con
 bool use_pair_gemm(int M, int N);
 void gemm_pair_f32(const CUtensorMap& A, const CUtensorMap& B, int M, int N, int K, const float* bias, float* out,
                    int ldo, int* err, cudaStream_t s);
+// The pair GEMMs' `rev` visits the 256-row blocks from the last one down (see
+// row_order_alternates); the results do not depend on it.
 // QKVs: q, k and v as one [3 x plane_rows][1024] block (k = q + plane_rows
 // rows, v = q + 2 plane_rows rows; v's fp16 bits moved as 16-bit elements)
 // with box 32 rows x 64 columns (the epilogue's TMA stores).
 void gemm_pair_qkv(const CUtensorMap& A, const CUtensorMap& B, const CUtensorMap& QKVs, int plane_rows, int M,
                    int b_off, const float* bias, bf16* q, bf16* k, __half* v, const int* pos, const float2* rope,
-                   int* err, cudaStream_t s);
+                   int* err, cudaStream_t s, bool rev = false);
 // Hs: h with box 32 rows x 64 columns (the epilogue's TMA stores).
 void gemm_pair_gelu(const CUtensorMap& A, const CUtensorMap& B, const CUtensorMap& Hs, int M, int b_off,
-                    const float* bias, bf16* h, int* err, cudaStream_t s);
+                    const float* bias, bf16* h, int* err, cudaStream_t s, bool rev = false);
 // X: the fp32 residual x with box 128 x 32 (loads); Xs: the same tensor with
 // box 32 x 32 (the epilogue's TMA stores of each warp's 32 rows).
 void gemm_pair_gate_res(const CUtensorMap& A, const CUtensorMap& B, const CUtensorMap& X, const CUtensorMap& Xs,
                         int M, int K, int b_off, const float* bias, const float* gate, float* x, int* err,
-                        cudaStream_t s);
+                        cudaStream_t s, bool rev = false);
 // causal grouped conv (k=31, 16 groups) over the staged rows [0, Ms); B box 64 x 64.
 // second == 0: out_stage[srow] = bf16(mish(conv + bias))  (rows with s2p >= 0)
 // second == 1: x[s2p[srow]] += mish(conv + bias)
@@ -168,7 +170,13 @@ bool attention(const CUtensorMap& Q, const CUtensorMap& K, const CUtensorMap& V,
 
 // ---- element-wise / row kernels -----------------------------------------
 // y = bf16(LN(x) * (1 + scale) + shift), rows of 1024 fp32.
-void adaln_rows(const float* x, bf16* y, const float* shift, const float* scale, int R, cudaStream_t s);
+// rev: rows visited from the last one down (see row_order_alternates).
+void adaln_rows(const float* x, bf16* y, const float* shift, const float* scale, int R, cudaStream_t s,
+                bool rev = false);
+// True unless LX_FLOW_ROW_ORDER=0: the decode alternates the row direction of
+// consecutive row-streaming kernels (AdaLN, the pair GEMMs) so that each one
+// starts on the rows its producer wrote last, which are still in L2.
+bool row_order_alternates();
 // x_state[f, c] += dt * (1.7 dphi[row_c] - 0.7 dphi[row_u]); xb rows <- bf16(x_state)
 void euler_update(float* xs, const float* dphi, const int2* frame_rows, bf16* xb, int F, float dt, float cfg,
                   cudaStream_t s);
