@@ -409,11 +409,21 @@ Plan make_plan(int n_utt, const int32_t* lengths, bool cfg_pairs, int chunk, int
   for (int s = 0; s < p.n_seq; ++s) {
     const int L = lengths[s / per];
     p.seq_len[s] = L;
-    p.seq_start[s] = r;
-    r += (L + SEQ_ALIGN - 1) / SEQ_ALIGN * SEQ_ALIGN;
     sr += STAGE_GAP;
     p.seq_sstart[s] = sr;
     sr += L;
+  }
+  // Packed rows: longest sequences first when the row direction alternates.
+  // Attention works longest first, so the rows it writes last (the shortest
+  // sequences) are the highest ones, which the out projection then reads
+  // first (it runs from the last row block down); see enqueue_dit.
+  std::vector<int> ord(p.n_seq);
+  for (int s = 0; s < p.n_seq; ++s) ord[s] = s;
+  if (row_order_alternates())
+    std::stable_sort(ord.begin(), ord.end(), [&p](int a, int b) { return p.seq_len[a] > p.seq_len[b]; });
+  for (const int s : ord) {
+    p.seq_start[s] = r;
+    r += (p.seq_len[s] + SEQ_ALIGN - 1) / SEQ_ALIGN * SEQ_ALIGN;
   }
   p.R = std::max(r, 1);
   p.Rs = std::max(sr, 1);
@@ -596,8 +606,9 @@ void enqueue_dit(lx_flow* h, const Plan& p, const float* mod, const float* mod_f
   const int i1024 = bn1024 == 256, iq = bnq == 256, iff = bnf == 256;
   const bool pair_q = use_pair_gemm(R, QKV_N), pair_f = use_pair_gemm(R, FF), pair_d = use_pair_gemm(R, DIM);
   // Row direction per kernel: each row-streaming kernel starts on the rows its
-  // producer wrote last (still in L2).  out (up) -> AdaLN (down) -> FF1 (up)
-  // -> FF2 (down) -> AdaLN (up) -> QKV (down); attention reads by work item.
+  // producer wrote last (still in L2).  attention (longest sequences, the
+  // lowest rows, first) -> out (down) -> AdaLN (up) -> FF1 (down) -> FF2 (up)
+  // -> AdaLN (down) -> QKV (up).
   const bool alt = row_order_alternates();
   int* err = h->d_err;
   timed(h, K_INPROJ, s, [&] { gemm_in_proj(bn1024, w.tm_xb, W.tm_winx[i1024], R, w.cst, w.x, w.stage1, w.p2s, err, s); });
@@ -611,11 +622,11 @@ void enqueue_dit(lx_flow* h, const Plan& p, const float* mod, const float* mod_f
   for (int l = 0; l < DEPTH; ++l) {
     // modulation chunks: shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp
     const float* m = mod + static_cast<size_t>(l) * MOD_N;
-    timed(h, K_ADALN, s, [&] { adaln_rows(w.x, w.xn, m + 0 * DIM, m + 1 * DIM, R, s); });
+    timed(h, K_ADALN, s, [&] { adaln_rows(w.x, w.xn, m + 0 * DIM, m + 1 * DIM, R, s, alt); });
     timed(h, K_QKV, s, [&] {
       if (pair_q)
         gemm_pair_qkv(w.tm_xn, W.tm_wqkv[0], w.tm_qkvs, static_cast<int>(w.capR), R, l * QKV_N,
-                      W.bqkv + static_cast<size_t>(l) * QKV_N, w.q, w.k, w.v, w.pos, W.rope, err, s, alt);
+                      W.bqkv + static_cast<size_t>(l) * QKV_N, w.q, w.k, w.v, w.pos, W.rope, err, s);
       else
         gemm_qkv(bnq, w.tm_xn, W.tm_wqkv[iq], R, l * QKV_N, W.bqkv + static_cast<size_t>(l) * QKV_N, w.q, w.k, w.v,
                  w.pos, W.rope, err, s);
@@ -625,22 +636,23 @@ void enqueue_dit(lx_flow* h, const Plan& p, const float* mod, const float* mod_f
     timed(h, K_OUT, s, [&] {
       if (pair_d)
         gemm_pair_gate_res(w.tm_ao, W.tm_wo[0], w.tm_x, w.tm_xs, R, DIM, l * DIM, W.bo + static_cast<size_t>(l) * DIM,
-                           m + 2 * DIM, w.x, err, s);
+                           m + 2 * DIM, w.x, err, s, alt);
       else
         gemm_gate_res_tma(w.tm_ao, W.tm_wo[0], w.tm_x, R, DIM, l * DIM, W.bo + static_cast<size_t>(l) * DIM,
                           m + 2 * DIM, w.x, err, s);
     });
-    timed(h, K_ADALN, s, [&] { adaln_rows(w.x, w.xn, m + 3 * DIM, m + 4 * DIM, R, s, alt); });
+    timed(h, K_ADALN, s, [&] { adaln_rows(w.x, w.xn, m + 3 * DIM, m + 4 * DIM, R, s); });
     timed(h, K_FF1, s, [&] {
       if (pair_f)
-        gemm_pair_gelu(w.tm_xn, W.tm_w1[0], w.tm_hs, R, l * FF, W.b1 + static_cast<size_t>(l) * FF, w.h, err, s);
+        gemm_pair_gelu(w.tm_xn, W.tm_w1[0], w.tm_hs, R, l * FF, W.b1 + static_cast<size_t>(l) * FF, w.h, err, s,
+                       alt);
       else
         gemm_gelu(bnf, w.tm_xn, W.tm_w1[iff], R, l * FF, W.b1 + static_cast<size_t>(l) * FF, w.h, err, s);
     });
     timed(h, K_FF2, s, [&] {
       if (pair_d)
         gemm_pair_gate_res(w.tm_h, W.tm_w2[0], w.tm_x, w.tm_xs, R, FF, l * DIM, W.b2 + static_cast<size_t>(l) * DIM,
-                           m + 5 * DIM, w.x, err, s, alt);
+                           m + 5 * DIM, w.x, err, s);
       else
         gemm_gate_res_tma(w.tm_h, W.tm_w2[0], w.tm_x, R, FF, l * DIM, W.b2 + static_cast<size_t>(l) * DIM,
                           m + 5 * DIM, w.x, err, s);
@@ -656,7 +668,7 @@ void enqueue_dit(lx_flow* h, const Plan& p, const float* mod, const float* mod_f
     }
   }
   // AdaLayerNormZero_Final: chunk order scale, shift (flow_reference.py:192)
-  timed(h, K_ADALN, s, [&] { adaln_rows(w.x, w.xn, mod_final + DIM, mod_final, R, s); });
+  timed(h, K_ADALN, s, [&] { adaln_rows(w.x, w.xn, mod_final + DIM, mod_final, R, s, alt); });
   timed(h, K_PROJOUT, s, [&] { gemm_f32(128, w.tm_xn, W.tm_wout, R, MEL, DIM, W.bout, w.dphi, MEL, err, s); });
   h->launches += 2;
   if (cap && cap->norm_out) {
