@@ -151,3 +151,39 @@ def test_cfg4_ctx500_streams_vs_oracle(dec):
     chunk + 6 look-ahead), block-causal chunk mask 50, 10-step CFG decode
     (8896 packed rows: QKV and FF1 on the pair kernel)."""
     _decode_vs_fixture(dec, CFG4, "oracle_cfg4_ctx500.npz")
+
+
+_ROW_ORDER_CHILD = r"""
+import sys
+import numpy as np
+repo, golden_dir, gguf, out_path = sys.argv[1:5]
+sys.path[:0] = [repo, golden_dir]
+from larynx_b200 import FlowDecoder
+from make_oracle_fixtures import parity_inputs
+lengths = [120, 700, 333, 1000, 250, 560]
+mus, conds, spks, noises = parity_inputs(lengths, seed=44)
+d = FlowDecoder(0)
+assert d.load(gguf), d.last_error
+np.save(out_path, d.decode(lengths, mus, conds, spks, noise=noises))
+d.close()
+"""
+
+
+def test_row_order_is_bit_identical(gguf_path, tmp_path):
+    """The decode packs sequences longest first and alternates the row
+    direction of AdaLN and the pair GEMMs (for L2 reuse between kernels);
+    with LX_FLOW_ROW_ORDER=0 it packs in input order and runs every kernel
+    upward.  Each row and tile is computed the same way in either order, so
+    the two decodes must agree bit for bit.  Every projection is forced onto
+    the pair kernel so that its reversed schedule runs (both switches are read
+    once per process, hence the child processes)."""
+    outs = {}
+    for v in ("0", "1"):
+        path = str(tmp_path / f"mel_{v}.npy")
+        env = dict(os.environ, LX_FLOW_ROW_ORDER=v, LX_FLOW_PAIR_GEMM="2")
+        r = subprocess.run([sys.executable, "-c", _ROW_ORDER_CHILD, REPO, GOLDEN, gguf_path, path],
+                           cwd=REPO, env=env, capture_output=True, text=True, timeout=600)
+        assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+        outs[v] = np.load(path)
+    assert np.isfinite(outs["1"]).all()
+    assert np.array_equal(outs["0"], outs["1"])
